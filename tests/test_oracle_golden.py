@@ -1,0 +1,117 @@
+"""Pin the CPU oracle against the reference's own outputs (golden fixtures).
+
+These run on CPU only.  They check that ``oracle/wgkv_oracle.py`` reproduces
+what the reference code produced in ``tests/golden/make_golden.py``:
+admission scores/masks, page tables, global lengths, pool contents, sparse
+indices, sparse-prefill rows and decode outputs.
+"""
+import numpy as np
+import pytest
+
+from golden_cases import O, PipelineCase, indices_case, load, regen_decode_inputs
+
+PIPELINES = ["c1_prefill", "promote_small", "defer_small"]
+
+
+@pytest.fixture(scope="module", params=PIPELINES)
+def case(request):
+    return PipelineCase(request.param)
+
+
+def test_sparse_indices_match_reference():
+    z = load("sparse_indices")
+    for i in range(int(z["n_cases"])):
+        (B, Hk, L, W, gs), g, fast, ref = indices_case(z, i)
+        mine = O.generate_sparse_indices(g, W, L)
+        for a, b in zip(mine, fast):
+            assert a.shape == b.shape and np.array_equal(a, b), f"case {i}"
+        mine_ref = O.generate_sparse_indices_ref(g, W, L)
+        for a, b in zip(mine_ref, ref):
+            assert a.shape == b.shape and np.array_equal(a, b), f"case {i}"
+        # the reference's own acceptance rule (utils/test_sparse_indices.py:30-46)
+        assert O.indices_equal(mine, ref)
+
+
+def test_paged_decode_matches_reference_oracle():
+    z = load("paged_decode")
+    for i in range(int(z["n_cases"])):
+        p = z[f"c{i}_params"]
+        q, kc, vc, sl, tbl = regen_decode_inputs(p)
+        o = O.paged_decode(q, kc, vc, sl, tbl, int(p[2]) ** -0.5)
+        # the reference oracle computes in bf16 (torch CPU); 2e-2 covers its rounding
+        np.testing.assert_allclose(o, z[f"c{i}_out"], atol=2e-2, rtol=1e-2)
+
+
+def test_gate_scores_match_reference(case):
+    total = mism = 0
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        s = O.gate_scores(case.params[l], pre_key=pk, post_key=k, value=v)
+        ref = case.ref_scores(l)
+        diff = O.bf16_bits(s) != O.bf16_bits(ref)
+        total += s.size
+        mism += int(diff.sum())
+        # masks: bit-exact required
+        assert np.array_equal(O.admission_mask(s, case.threshold), case.ref_mask(l))
+    # scores: identical bf16 except for rare 1-ulp accumulation-order differences
+    assert mism <= max(2, total // 2000), (mism, total)
+
+
+def test_prefill_state_matches_reference(case):
+    st = case.new_state()
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        st.prefill_layer(l, k, v, case.ref_mask(l), pre_key=pk)
+    z = case.z
+    assert np.array_equal(st.block_table[:, 0], z["prefill_block_table"])
+    assert np.array_equal(st.global_lengths[:, 0], z["prefill_global_lengths"])
+    assert np.array_equal(st.local_is_global[:, 0], z["prefill_local_is_global"])
+    assert st.next_free_block == int(z["prefill_next_free_block"])
+    dig = O.pool_digest(st.block_table, st.global_lengths, st.local_length,
+                        O.bf16_bits(st.k), O.bf16_bits(st.v), st.page, st.window)
+    assert np.array_equal(dig, z["prefill_pool_sha"])
+
+
+def test_prefill_indices_and_attention_rows(case):
+    L = case.L
+    rows = np.arange(L - case.rows_out, L)
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        g = case.ref_mask(l)
+        idx = O.generate_sparse_indices(g, case.W, L)
+        for a, n in zip(idx, ("bc", "bo", "cc", "ci")):
+            assert np.array_equal(a, case.z[f"l{l}_{n}"])
+        m1 = O.sparse_mask_from_indices(*idx, L, case.G, rows=rows)
+        m2 = O.ideal_mask(g, case.W, L, rows=rows)
+        assert np.array_equal(m1, m2)
+        o = O.masked_attention(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3), m1, rows=rows)
+        np.testing.assert_allclose(o[0], case.z[f"l{l}_attn_rows"], atol=1e-5, rtol=1e-5)
+
+
+def test_decode_steps_match_reference(case):
+    st = case.new_state()
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        st.prefill_layer(l, k, v, case.ref_mask(l), pre_key=pk)
+    z = case.z
+    gate = lambda l: (lambda pre, post, val: O.gate_scores(case.params[l], pre_key=pre, post_key=post, value=val))
+    for s in range(case.n_decode):
+        for l in range(case.Ly):
+            q, k, v, pk = case.decode[s][l]
+            if l == 0 and st.local_length == st.window:
+                st.promote()
+            gm = case.ref_decode_mask(s, l)
+            cur = st.append_layer(l, k[:, :, 0], v[:, :, 0], None if gm is None else gm[:, :, 0],
+                                  pre_key_new=pk[:, :, 0], gate_fn=gate(l), threshold=case.threshold)
+            sl, bt = st.decode_tables(l, cur)
+            kc, vc = st.paged_views()
+            o = O.paged_decode(q.transpose(0, 2, 1, 3), kc, vc, sl, bt, case.D ** -0.5)
+            np.testing.assert_allclose(o[0, 0], z[f"d{s}_l{l}_out"], atol=2e-2, rtol=1e-2)
+        assert np.array_equal(st.block_table[:, 0], z[f"d{s}_block_table"]), s
+        assert np.array_equal(st.global_lengths[:, 0], z[f"d{s}_global_lengths"]), s
+        assert np.array_equal(st.local_is_global[:, 0], z[f"d{s}_local_is_global"]), s
+        assert st.next_free_block == int(z[f"d{s}_next_free_block"])
+        assert st.local_ptr == int(z[f"d{s}_local_ptr"]) and st.local_length == int(z[f"d{s}_local_length"])
+        dig = O.pool_digest(st.block_table, st.global_lengths, st.local_length,
+                            O.bf16_bits(st.k), O.bf16_bits(st.v), st.page, st.window)
+        assert np.array_equal(dig, z[f"d{s}_pool_sha"]), s
