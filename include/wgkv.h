@@ -57,6 +57,138 @@ WGKV_API int wgkv_version(void);
 /* Number of SMs of the current device (cached per device). <0 on error. */
 WGKV_API int wgkv_num_sms(void);
 
+/* ---- paged pool state (shared by the admission entry points) ------------ */
+/*
+ * Device-resident state that the reference attaches to its DynamicCache in
+ * prefill_wrapper (modeling_layers.py:1196-1288), with a batch axis added.
+ * Layout (batch 1 reproduces the reference exactly):
+ *   k, v             (total_blocks * page, head_dim) bf16 rows; page p = rows [p*page, (p+1)*page)
+ *   block_table      (layers, batch, kv_heads, max_blocks_per_head) int32; entries [0, window/page) are
+ *                    the ring pages, global pages follow; unused entries hold total_blocks - 1
+ *   global_lengths   (layers, batch, kv_heads) int32
+ *   local_is_global  (layers, batch, kv_heads, window) uint8
+ *   local_pre_key    (layers, batch, kv_heads, window, head_dim) bf16, deferred gating only (else NULL)
+ *   next_free_block  device int32 scalar: bump allocator of global pages
+ *   err              device int32 error word (WGKV_ERR_* bits)
+ * The ring slot s of (layer l, batch b, head h) is pool row ((l*batch + b)*kv_heads + h)*window + s.
+ */
+typedef struct wgkv_pool {
+  uint16_t* k;
+  uint16_t* v;
+  int32_t* block_table;
+  int32_t* global_lengths;
+  uint8_t* local_is_global;
+  uint16_t* local_pre_key;
+  int32_t* next_free_block;
+  int* err;
+  int64_t total_blocks;
+  int32_t layers;
+  int32_t batch;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t window;
+  int32_t page;
+  int32_t max_blocks_per_head;
+  int32_t max_tokens_per_head;
+} wgkv_pool;
+
+/* ---- (a1, a2) write gate + admission mask --------------------------------- */
+/*
+ * scores[b,h,t] = bf16(sigmoid(w2_h . act(W1_h x + b1_h) + b2_h)), mask = scores > threshold,
+ * x = concat of the inputs selected by `input_mask` (bit 0 pre_k, bit 1 post_k, bit 2 value, in that
+ * order), each optionally RMS-normalised with its row of `norm_w` (3, D) when norm_w != NULL.  Rounds
+ * to bf16 where the reference's bf16 tensors do (GatingPredictor fast path, :170-196); GEMM
+ * accumulation is fp32.  Inputs are (B, Hk, L, D) with element strides (sb, sh, st); unused inputs
+ * may be NULL.  w1 (Hk, inner, I), b1 (Hk, inner), w2 (Hk, inner), b2 (Hk) bf16.  Either output may
+ * be NULL; strides are in elements.  act: 0 GELU (erf), 1 SiLU.
+ * Constraints: D in {64, 128}; inner % 8 == 0; I = D * popcount(input_mask) <= 384.
+ */
+WGKV_API int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
+                              const uint16_t* post_k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                              const uint16_t* value, int64_t v_sb, int64_t v_sh, int64_t v_st, int batch,
+                              int kv_heads, int seq_len, int head_dim, int input_mask, const uint16_t* w1,
+                              const uint16_t* b1, const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w,
+                              float rms_eps, int inner, int act, float threshold, uint16_t* scores, int64_t s_sb,
+                              int64_t s_sh, int64_t s_st, uint8_t* mask, int64_t m_sb, int64_t m_sh, int64_t m_st,
+                              void* stream);
+
+/* ---- (a3) prefill: ring fill + admission compaction ----------------------- */
+/*
+ * For every (b, h) of `layer`: the last min(L, window) tokens go to ring slots 0.. (with their mask
+ * bits into local_is_global, and pre_k into local_pre_key when the pool has it); the admitted tokens
+ * among the first L - window are packed, in token order, into freshly allocated contiguous global
+ * pages.  Pages are allocated from next_free_block in (b, h) order, so batch 1 reproduces the
+ * reference's page ids.  On a capacity violation nothing of the layer is written and err gets
+ * WGKV_ERR_HEAD_CAPACITY / WGKV_ERR_POOL_EXHAUSTED (reference asserts :1313-1321).
+ * k, v, pre_k: (B, Hk, L, D) strided; g_mask (B, Hk, L) uint8 strided.
+ */
+WGKV_API size_t wgkv_prefill_admit_workspace_size(int batch, int kv_heads, int seq_len);
+WGKV_API int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len, const uint16_t* k, int64_t k_sb,
+                                int64_t k_sh, int64_t k_st, const uint16_t* v, int64_t v_sb, int64_t v_sh,
+                                int64_t v_st, const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
+                                const uint8_t* g_mask, int64_t m_sb, int64_t m_sh, int64_t m_st, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* ---- (a4) lazy promotion ---------------------------------------------------- */
+/*
+ * For every (layer, b, h) whose ring slot `local_ptr` is admitted: append that slot's K/V to the
+ * head's global pages (a new page from next_free_block when the length is a multiple of `page`,
+ * allocated in (layer, b, h) order) and bump global_lengths.  One launch for all layers, as the
+ * reference does at layer 0 when the ring is full (:1470-1471).  Capacity violations write nothing
+ * and set err.
+ */
+WGKV_API int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream);
+
+/* ---- (a5, a6) decode: ring append + attention lengths --------------------- */
+/*
+ * Writes k_new/v_new (B, Hk, D; strides sb, sh) into ring slot `insert_pos` of `layer`, pre_k_new into
+ * local_pre_key when non-NULL, and cache_seqlens[b, h] = cur_local_len + global_lengths[layer, b, h]
+ * (modeling_layers.py:1390-1400, :1429-1432).  The admission bit of the new token is written by
+ * wgkv_gate_scores straight into local_is_global.
+ */
+WGKV_API int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
+                                int64_t v_sb, int64_t v_sh, const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh,
+                                int32_t* cache_seqlens, void* stream);
+
+/* ---- (a9-a11) vertical-slash sparse indices -------------------------------- */
+/*
+ * generate_sparse_indices (:385-409) on the device.  Outputs (R = ceil(L / block), P = min(W/block, R)):
+ *   block_count (R) int32, block_offset (R, P+1) int32  -- generate_block_offset :321-349
+ *   column_count (B, Hk, R) int32, column_index (B, Hk, ci_stride) int32 -- generate_column_index
+ *   :352-381: column_index holds every admitted token index in ascending order (entries past the
+ *   head's count are left untouched), column_count[i] = #admitted < block*(i-P)+1 for i >= P, else 0.
+ *   max_count (device int32, may be NULL) receives max over (b, h) of the admitted count (Gmax, :369),
+ *   as an atomicMax: zero it first.  ci_stride must be >= L.  Requires window % block == 0.
+ */
+WGKV_API size_t wgkv_sparse_indices_workspace_size(int batch, int kv_heads, int seq_len);
+WGKV_API int wgkv_sparse_indices(const uint8_t* g_mask, int64_t m_sb, int64_t m_sh, int64_t m_st, int batch,
+                                 int kv_heads, int seq_len, int window, int block, int32_t* block_count,
+                                 int32_t* block_offset, int32_t* column_count, int32_t* column_index,
+                                 int64_t ci_stride, int32_t* max_count, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* ---- (a12) block-sparse causal prefill attention --------------------------- */
+/*
+ * out[b, q, hq, :] = softmax over keys k of (q . k * scale) V, where k ranges over the union of
+ *   - the band blocks [block_offset[i, c], block_offset[i, c] + block) for c < block_count[i], and
+ *   - the admitted columns column_index[b, h, 0, 0 .. column_count[b, h, i]),
+ * intersected with k <= q (causal), i = q / block, h = hq / (Hq / Hk).  This is the attention that
+ * sparse_attn_func computes for the indices of generate_sparse_indices (as pinned by
+ * utils/test_sparse_attn.py:34-93); band and column sets are disjoint for such indices.
+ *   q   (B, L, Hq, D) bf16, strides (sb, sl, sh) in elements (last axis contiguous)
+ *   k,v (B, L, Hk, D) bf16, strides likewise; out (B, L, Hq, D) bf16 strided likewise
+ *   block_count (R), block_offset (R, bo_stride), column_count (B, Hk, R), column_index (B, Hk, ci_stride)
+ * Constraints: D in {64, 128}; block == 64; Hq % Hk == 0.
+ */
+WGKV_API int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const uint16_t* k,
+                                 int64_t k_sb, int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb,
+                                 int64_t v_sl, int64_t v_sh, int batch, int seq_len, int num_q_heads,
+                                 int num_kv_heads, int head_dim, const int32_t* block_count,
+                                 const int32_t* block_offset, int64_t bo_stride, const int32_t* column_count,
+                                 const int32_t* column_index, int64_t ci_stride, float softmax_scale, uint16_t* out,
+                                 int64_t o_sb, int64_t o_sl, int64_t o_sh, void* stream);
+
 /* ---- (a7, a8) ragged paged decode attention ----------------------------- */
 /*
  * out[b, 0, hq, :] = softmax(q[b, 0, hq, :] . K_h^T * scale) V_h, h = hq / G,

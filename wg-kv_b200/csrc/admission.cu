@@ -1,0 +1,565 @@
+// Write gate, admission compaction, ring append and lazy promotion (sm_100a).
+//
+// Reference: src/modeling_layers.py -- GatingPredictor.forward fast path
+// (:170-196), the threshold (:1465), prefill_wrapper's ring fill and per-head
+// compaction (:1290-1331, a host loop with torch.where + .item() syncs),
+// migrate_local_kv_to_global (:674-763, nonzero + .item()), and
+// decode_wrapper's ring append (:1390-1413).  Here every step is a device
+// kernel with no host synchronisation: counts are reduced per 2048-token
+// chunk with warp ballots, scanned on the device, and pages are handed out by
+// a device-side bump allocator in the reference's (layer, batch, head) order
+// so the page tables come out identical.
+#include "common.cuh"
+#include "runtime.h"
+#include "scan.cuh"
+
+namespace wgkv {
+namespace {
+
+// ============================================================================
+// gate: bf16 2-layer MLP per (b, h, t) on mma.sync tensor cores
+// ============================================================================
+constexpr int kGateRows = 128;   // rows (tokens) per CTA
+constexpr int kGateThreads = 256;  // 8 warps x 16 rows
+constexpr int kGateChunk = 64;   // W1 rows (hidden neurons) per shared-memory chunk
+
+struct GateParams {
+  const uint16_t* in[3];
+  int64_t sb[3], sh[3], st[3];
+  const uint16_t* norm[3];
+  int n_in;
+  int B, Hk, L, D, I, inner, act;
+  const uint16_t *w1, *b1, *w2, *b2;
+  float eps, thr;
+  uint16_t* scores;
+  int64_t ssb, ssh, sst;
+  uint8_t* mask;
+  int64_t msb, msh, mst;
+};
+
+WGKV_DEV float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
+WGKV_DEV uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
+WGKV_DEV float act_fn(float x, int act) {
+  if (act == 1) return x / (1.f + expf(-x));             // nn.SiLU
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));  // nn.GELU() (erf form)
+}
+
+__global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int I = p.I, RS = I + 8;  // padded row stride (elements): conflict-free ldmatrix
+  uint16_t* xs = reinterpret_cast<uint16_t*>(sm);
+  uint16_t* ws = xs + kGateRows * RS;
+  float* b1s = reinterpret_cast<float*>(ws + kGateChunk * RS);
+  float* w2s = b1s + kGateChunk;
+  const int h = blockIdx.y;
+  const int row0 = blockIdx.x * kGateRows;
+  const int nrows = p.B * p.L;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- stage the input rows (concat + optional RMS norm) as bf16 ----------
+  const int per = p.D / 32;  // elements per lane per input (2 or 4)
+  for (int r = warp; r < kGateRows; r += kGateThreads / 32) {
+    const int gr = row0 + r;
+    uint16_t* dst = xs + r * RS;
+    if (gr >= nrows) {
+      for (int e = lane; e < I; e += 32) dst[e] = 0;
+      continue;
+    }
+    const int b = gr / p.L, t = gr - b * p.L;
+    for (int s = 0; s < p.n_in; ++s) {
+      const uint16_t* src = p.in[s] + b * p.sb[s] + h * p.sh[s] + int64_t(t) * p.st[s];
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        if (j < per) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(src + lane * per + j);
+          x[j] = __uint_as_float(w << 16);
+          x[j + 1] = __uint_as_float(w & 0xffff0000u);
+        }
+      }
+      if (p.norm[s]) {
+        // GatingRMSNorm.forward (:123-128): fp32 variance, x * rsqrt(var + eps) -> bf16, * weight -> bf16
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss += x[j] * x[j];  // x[j] = 0 past `per`
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+        const float inv = 1.f / sqrtf(ss / float(p.D) + p.eps);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (j < per) {
+            const float y = bf16_round(x[j] * inv);
+            x[j] = bf16_round(bf2f(p.norm[s][lane * per + j]) * y);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j += 2)
+        if (j < per) *reinterpret_cast<uint32_t*>(dst + s * p.D + lane * per + j) = pack_bf16x2(x[j], x[j + 1]);
+    }
+  }
+
+  const int g = lane >> 2, t4 = lane & 3, mi = lane >> 3, ri = lane & 7;
+  float part0 = 0.f, part1 = 0.f;
+  const uint16_t* w1h = p.w1 + int64_t(h) * p.inner * I;
+  for (int n0 = 0; n0 < p.inner; n0 += kGateChunk) {
+    __syncthreads();
+    // W1 rows n0 .. n0+63 (zero past inner), 16-byte vectors
+    const int vec_per_row = I / 8;
+    for (int e = tid; e < kGateChunk * vec_per_row; e += kGateThreads) {
+      const int j = e / vec_per_row, c = e - j * vec_per_row;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (n0 + j < p.inner) v = *reinterpret_cast<const uint4*>(w1h + int64_t(n0 + j) * I + c * 8);
+      *reinterpret_cast<uint4*>(ws + j * RS + c * 8) = v;
+    }
+    if (tid < kGateChunk) {
+      const bool ok = n0 + tid < p.inner;
+      b1s[tid] = ok ? bf2f(p.b1[h * p.inner + n0 + tid]) : 0.f;
+      w2s[tid] = ok ? bf2f(p.w2[h * p.inner + n0 + tid]) : 0.f;
+    }
+    __syncthreads();
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const uint32_t xbase = smem_u32(xs + (warp * 16 + (mi & 1) * 8 + ri) * RS + (mi >> 1) * 8);
+    const uint32_t wbase = smem_u32(ws + ((mi >> 1) * 8 + ri) * RS + (mi & 1) * 8);
+    for (int kk = 0; kk < I / 16; ++kk) {
+      uint32_t a[4];
+      ldmatrix_x4(a[0], a[1], a[2], a[3], xbase + kk * 32);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4(r0, r1, r2, r3, wbase + (np * 16 * RS) * 2 + kk * 32);
+        mma_bf16_16816(acc[2 * np], a, r0, r1);
+        mma_bf16_16816(acc[2 * np + 1], a, r2, r3);
+      }
+    }
+    // epilogue: bf16(h) -> bf16(h + b1) -> bf16(act) -> fp32 dot with w2
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int n = j * 8 + 2 * t4 + e;
+        const float bb = b1s[n], ww = w2s[n];
+        float h0 = bf16_round(bf16_round(acc[j][e]) + bb);
+        float h1 = bf16_round(bf16_round(acc[j][2 + e]) + bb);
+        part0 += bf16_round(act_fn(h0, p.act)) * ww;
+        part1 += bf16_round(act_fn(h1, p.act)) * ww;
+      }
+    }
+  }
+  part0 += __shfl_xor_sync(0xffffffff, part0, 1);
+  part0 += __shfl_xor_sync(0xffffffff, part0, 2);
+  part1 += __shfl_xor_sync(0xffffffff, part1, 1);
+  part1 += __shfl_xor_sync(0xffffffff, part1, 2);
+  if (t4 == 0) {
+    const float b2 = bf2f(p.b2[h]);
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int gr = row0 + warp * 16 + g + rr * 8;
+      if (gr >= nrows) continue;
+      const int b = gr / p.L, t = gr - b * p.L;
+      float o = bf16_round(rr ? part1 : part0);
+      o = bf16_round(o + b2);
+      const float s = bf16_round(1.f / (1.f + expf(-o)));
+      if (p.scores) p.scores[b * p.ssb + h * p.ssh + int64_t(t) * p.sst] = f2bf(s);
+      if (p.mask) p.mask[b * p.msb + h * p.msh + int64_t(t) * p.mst] = s > p.thr ? 1 : 0;
+    }
+  }
+}
+
+// ============================================================================
+// prefill compaction
+// ============================================================================
+struct PoolArgs {
+  wgkv_pool P;
+};
+
+// Single CTA: per-head chunk scans, page allocation in (b, h) order, table writes.
+__global__ void __launch_bounds__(1024) prefill_alloc_kernel(PoolArgs pa, int layer, int nch, int n_loc,
+                                                             int* counts, int* totals, int* first, int* okflag) {
+  const wgkv_pool& P = pa.P;
+  const int BH = P.batch * P.kv_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int bh = warp; bh < BH; bh += 32) {
+    int carry = 0;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const int c = c0 + lane;
+      const int v = c < nch ? counts[bh * nch + c] : 0;
+      int x = v;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffff, x, o);
+        if (lane >= o) x += y;
+      }
+      if (c < nch) counts[bh * nch + c] = carry + x - v;
+      carry += __shfl_sync(0xffffffff, x, 31);
+    }
+    if (lane == 0) totals[bh] = carry;
+  }
+  __syncthreads();
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const int nf = *P.next_free_block;
+    int64_t run = 0;
+    int ok = 1;
+    for (int bh = 0; bh < BH; ++bh) {
+      const int n = totals[bh];
+      if (n > 0 && n_loc + n > P.max_tokens_per_head) {
+        set_error(P.err, WGKV_ERR_HEAD_CAPACITY);
+        ok = 0;
+      }
+      first[bh] = int(nf + run);
+      run += (n + P.page - 1) / P.page;
+    }
+    if (nf + run > P.total_blocks) {
+      set_error(P.err, WGKV_ERR_POOL_EXHAUSTED);
+      ok = 0;
+    }
+    if (ok) *P.next_free_block = int(nf + run);
+    *okflag = ok;
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int lp = P.window / P.page;
+  for (int bh = warp; bh < BH; bh += 32) {
+    const int n = totals[bh];
+    const int need = (n + P.page - 1) / P.page;
+    int32_t* trow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head + lp;
+    for (int j = lane; j < need; j += 32) trow[j] = first[bh] + j;
+    if (lane == 0) P.global_lengths[layer * BH + bh] = n;
+  }
+}
+
+struct RowSrc {
+  const uint16_t* p;
+  int64_t sb, sh, st;
+};
+
+template <bool kVec16>
+WGKV_DEV void copy_row(uint16_t* dst, const uint16_t* src, int D, int lane_in_group, int group_size) {
+  if (kVec16) {
+    for (int c = lane_in_group; c < D / 8; c += group_size)
+      reinterpret_cast<uint4*>(dst)[c] = *reinterpret_cast<const uint4*>(src + c * 8);
+  } else {
+    for (int c = lane_in_group; c < D / 2; c += group_size)
+      reinterpret_cast<uint32_t*>(dst)[c] = *reinterpret_cast<const uint32_t*>(src + c * 2);
+  }
+}
+
+template <bool kVec16>
+__global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs pa, int layer, int L, int n_early,
+                                                                       int n_loc, int nch, MaskView mv, RowSrc K,
+                                                                       RowSrc V, RowSrc PK, const int* counts,
+                                                                       const int* first, const int* okflag) {
+  if (!*okflag) return;
+  const wgkv_pool& P = pa.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk, c = blockIdx.x;
+  __shared__ int2 list[kChunk];  // (token, -2 - ring slot for ring rows)
+  __shared__ int wsum[kScanThreads / 32];
+  __shared__ int s_n;
+  const int t0 = c * kChunk + threadIdx.x * 8;
+  const int ring_start = L - n_loc;  // first token that goes to the ring
+  const int64_t ring_row0 = (int64_t(layer) * BH + bh) * P.window;
+  uint8_t mk[8];
+  int ng = 0, nr = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int t = t0 + j;
+    mk[j] = t < L ? mv.at(b, h, t) : 0;
+    ng += (t < n_early && mk[j]) ? 1 : 0;
+    nr += (t < L && t >= ring_start) ? 1 : 0;
+  }
+  int tot;
+  const int gbase = block_excl_scan(ng, wsum, tot);
+  int rtot;
+  const int rbase = block_excl_scan(nr, wsum, rtot);
+  const int chunk_off = (c < nch) ? counts[bh * nch + c] : 0;
+  const int64_t gdst0 = int64_t(first[bh]) * P.page + chunk_off;
+  int gi = gbase, ri = rbase;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int t = t0 + j;
+    if (t < n_early && mk[j]) {
+      list[gi] = make_int2(t, 0);  // destination = gdst0 + list index
+      ++gi;
+    } else if (t < L && t >= ring_start) {
+      const int slot = t - ring_start;
+      list[tot + ri] = make_int2(t, -2 - slot);  // ring rows encoded as -2 - slot
+      P.local_is_global[ring_row0 + slot] = mk[j];
+      ++ri;
+    }
+  }
+  if (threadIdx.x == 0) s_n = tot + rtot;
+  __syncthreads();
+  const int n = s_n;
+  // copy rows: one warp-quarter (8 lanes) per row
+  const int grp = threadIdx.x >> 3, gl = threadIdx.x & 7;
+  for (int e = grp; e < n; e += kScanThreads / 8) {
+    const int t = list[e].x;
+    int64_t dst;
+    const bool ring = e >= tot;
+    if (ring) dst = ring_row0 + (-2 - list[e].y);
+    else dst = gdst0 + e;
+    const int64_t so_k = b * K.sb + h * K.sh + int64_t(t) * K.st;
+    const int64_t so_v = b * V.sb + h * V.sh + int64_t(t) * V.st;
+    copy_row<kVec16>(P.k + dst * D, K.p + so_k, D, gl, 8);
+    copy_row<kVec16>(P.v + dst * D, V.p + so_v, D, gl, 8);
+    if (ring && P.local_pre_key && PK.p) {
+      const int64_t so_p = b * PK.sb + h * PK.sh + int64_t(t) * PK.st;
+      copy_row<kVec16>(P.local_pre_key + dst * D, PK.p + so_p, D, gl, 8);
+    }
+  }
+}
+
+// ============================================================================
+// decode: ring append + cache_seqlens
+// ============================================================================
+__global__ void __launch_bounds__(256) decode_append_kernel(PoolArgs pa, int layer, int ins, int cur, RowSrc K,
+                                                            RowSrc V, RowSrc PK, int32_t* cache_seqlens) {
+  const wgkv_pool& P = pa.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
+  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= BH) return;
+  const int b = i / Hk, h = i - b * Hk;
+  const int64_t row = (int64_t(layer) * BH + i) * P.window + ins;
+  copy_row<false>(P.k + row * D, K.p + b * K.sb + h * K.sh, D, lane, 32);
+  copy_row<false>(P.v + row * D, V.p + b * V.sb + h * V.sh, D, lane, 32);
+  if (PK.p && P.local_pre_key) copy_row<false>(P.local_pre_key + row * D, PK.p + b * PK.sb + h * PK.sh, D, lane, 32);
+  if (lane == 0 && cache_seqlens) cache_seqlens[i] = cur + P.global_lengths[layer * BH + i];
+}
+
+// ============================================================================
+// lazy promotion (migrate_local_kv_to_global)
+// ============================================================================
+__global__ void __launch_bounds__(1024) promote_kernel(PoolArgs pa, int ptr) {
+  const wgkv_pool& P = pa.P;
+  const int N = P.layers * P.batch * P.kv_heads;
+  const int W = P.window, T = P.page, D = P.head_dim;
+  __shared__ int s_cnt, s_ovf, s_nf;
+  __shared__ int wsum[32];
+  if (threadIdx.x == 0) { s_cnt = 0; s_ovf = 0; }
+  __syncthreads();
+  int cnt = 0, ovf = 0;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    if (P.local_is_global[int64_t(i) * W + ptr]) {
+      const int gl = P.global_lengths[i];
+      if (W + gl + 1 > P.max_tokens_per_head) ovf = 1;
+      cnt += (gl % T) == 0;
+    }
+  }
+  atomicAdd(&s_cnt, cnt);
+  if (ovf) atomicOr(&s_ovf, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nf = *P.next_free_block;
+    s_nf = nf;
+    if (s_ovf) {
+      set_error(P.err, WGKV_ERR_HEAD_CAPACITY);
+      s_ovf = 1;
+    } else if (int64_t(nf) + s_cnt > P.total_blocks) {
+      set_error(P.err, WGKV_ERR_POOL_EXHAUSTED);
+      s_ovf = 1;
+    } else {
+      *P.next_free_block = nf + s_cnt;
+    }
+  }
+  __syncthreads();
+  if (s_ovf) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int carry = s_nf;
+  for (int base = 0; base < N; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    int flag = 0, gl = 0;
+    if (i < N) {
+      flag = P.local_is_global[int64_t(i) * W + ptr];
+      if (flag) gl = P.global_lengths[i];
+    }
+    const int need = flag && (gl % T) == 0;
+    // block exclusive scan of `need` in (layer, b, h) order
+    int x = need;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffff, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    int wb = 0, tot = 0;
+    for (int w = 0; w < nw; ++w) {
+      if (w < warp) wb += wsum[w];
+      tot += wsum[w];
+    }
+    __syncthreads();
+    if (flag) {
+      int32_t* trow = P.block_table + int64_t(i) * P.max_blocks_per_head + W / T;
+      int pid;
+      if (need) {
+        pid = carry + wb + x - need;
+        trow[gl / T] = pid;
+      } else {
+        pid = trow[gl / T];
+      }
+      const int64_t dst = int64_t(pid) * T + gl % T;
+      const int64_t src = int64_t(i) * W + ptr;
+      for (int c = 0; c < D / 8; ++c) {
+        reinterpret_cast<uint4*>(P.k + dst * D)[c] = reinterpret_cast<const uint4*>(P.k + src * D)[c];
+        reinterpret_cast<uint4*>(P.v + dst * D)[c] = reinterpret_cast<const uint4*>(P.v + src * D)[c];
+      }
+      P.global_lengths[i] = gl + 1;
+    }
+    carry += tot;
+  }
+}
+
+bool pool_ok(const wgkv_pool* P) {
+  return P && P->k && P->v && P->block_table && P->global_lengths && P->local_is_global && P->next_free_block &&
+         P->layers > 0 && P->batch > 0 && P->kv_heads > 0 && (P->head_dim == 64 || P->head_dim == 128) &&
+         P->page > 0 && P->window > 0 && P->window % P->page == 0 && P->total_blocks > 0;
+}
+
+}  // namespace
+}  // namespace wgkv
+
+using namespace wgkv;
+
+extern "C" int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
+                                const uint16_t* post_k, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                                const uint16_t* value, int64_t v_sb, int64_t v_sh, int64_t v_st, int batch,
+                                int kv_heads, int seq_len, int head_dim, int input_mask, const uint16_t* w1,
+                                const uint16_t* b1, const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w,
+                                float rms_eps, int inner, int act, float threshold, uint16_t* scores, int64_t s_sb,
+                                int64_t s_sh, int64_t s_st, uint8_t* mask, int64_t m_sb, int64_t m_sh, int64_t m_st,
+                                void* stream) {
+  if (batch <= 0 || kv_heads <= 0 || seq_len < 0 || (head_dim != 64 && head_dim != 128)) return WGKV_EINVAL;
+  if (inner <= 0 || inner % 8 != 0 || !w1 || !b1 || !w2 || !b2 || (act != 0 && act != 1)) return WGKV_EINVAL;
+  if (seq_len == 0) return WGKV_OK;
+  GateParams p = {};
+  const uint16_t* ins[3] = {pre_k, post_k, value};
+  const int64_t sbs[3] = {pk_sb, k_sb, v_sb}, shs[3] = {pk_sh, k_sh, v_sh}, sts[3] = {pk_st, k_st, v_st};
+  int n = 0;
+  for (int s = 0; s < 3; ++s) {
+    if (!(input_mask & (1 << s))) continue;
+    if (!ins[s] || (reinterpret_cast<uintptr_t>(ins[s]) & 3) || (sbs[s] | shs[s] | sts[s]) & 1) return WGKV_EINVAL;
+    p.in[n] = ins[s];
+    p.sb[n] = sbs[s];
+    p.sh[n] = shs[s];
+    p.st[n] = sts[s];
+    p.norm[n] = norm_w ? norm_w + s * head_dim : nullptr;
+    ++n;
+  }
+  if (n == 0 || n * head_dim > 384) return WGKV_EINVAL;
+  if (reinterpret_cast<uintptr_t>(w1) & 15) return WGKV_EINVAL;
+  p.n_in = n;
+  p.B = batch;
+  p.Hk = kv_heads;
+  p.L = seq_len;
+  p.D = head_dim;
+  p.I = n * head_dim;
+  p.inner = inner;
+  p.act = act;
+  p.w1 = w1;
+  p.b1 = b1;
+  p.w2 = w2;
+  p.b2 = b2;
+  p.eps = rms_eps;
+  p.thr = threshold;
+  p.scores = scores;
+  p.ssb = s_sb;
+  p.ssh = s_sh;
+  p.sst = s_st;
+  p.mask = mask;
+  p.msb = m_sb;
+  p.msh = m_sh;
+  p.mst = m_st;
+  const int RS = p.I + 8;
+  const size_t smem = size_t(kGateRows + kGateChunk) * RS * 2 + 2 * kGateChunk * 4;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+      return WGKV_ECUDA;
+    attr[dev] = true;
+  }
+  dim3 grid((int64_t(batch) * seq_len + kGateRows - 1) / kGateRows, kv_heads);
+  gate_kernel<<<grid, kGateThreads, smem, as_stream(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+static int nchunks(int n) { return n > 0 ? (n + kChunk - 1) / kChunk : 0; }
+
+extern "C" size_t wgkv_prefill_admit_workspace_size(int batch, int kv_heads, int seq_len) {
+  const size_t BH = size_t(batch) * kv_heads;
+  return (BH * (nchunks(seq_len) + 2) + 64) * 4;
+}
+
+extern "C" int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len, const uint16_t* k, int64_t k_sb,
+                                  int64_t k_sh, int64_t k_st, const uint16_t* v, int64_t v_sb, int64_t v_sh,
+                                  int64_t v_st, const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
+                                  const uint8_t* g_mask, int64_t m_sb, int64_t m_sh, int64_t m_st, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || seq_len <= 0 || !k || !v || !g_mask || !workspace)
+    return WGKV_EINVAL;
+  const int BH = pool->batch * pool->kv_heads;
+  const int W = pool->window;
+  const int n_loc = seq_len < W ? seq_len : W;
+  const int n_early = seq_len - W;  // tokens eligible for the global cache
+  const int nch = nchunks(n_early);
+  if (workspace_bytes < wgkv_prefill_admit_workspace_size(pool->batch, pool->kv_heads, n_early > 0 ? n_early : 0))
+    return WGKV_ENOSPC;
+  int* counts = reinterpret_cast<int*>(workspace);
+  int* totals = counts + size_t(BH) * nch;
+  int* first = totals + BH;
+  int* okflag = first + BH;
+  cudaStream_t s = as_stream(stream);
+  MaskView mv{g_mask, m_sb, m_sh, m_st};
+  if (nch > 0) {
+    chunk_count_kernel<<<dim3(nch, BH), kScanThreads, 0, s>>>(mv, pool->kv_heads, n_early, nch, counts);
+  }
+  PoolArgs pa{*pool};
+  prefill_alloc_kernel<<<1, 1024, 0, s>>>(pa, layer, nch, n_loc, counts, totals, first, okflag);
+  const int D = pool->head_dim;
+  const bool vec16 = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                       reinterpret_cast<uintptr_t>(pre_k)) & 15) == 0 &&
+                     ((k_sb | k_sh | k_st | v_sb | v_sh | v_st) % 8 == 0) &&
+                     (!pre_k || (pk_sb | pk_sh | pk_st) % 8 == 0);
+  if (((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 3) || ((k_sb | k_sh | k_st | v_sb | v_sh | v_st) & 1))
+    return WGKV_EINVAL;
+  (void)D;
+  RowSrc K{k, k_sb, k_sh, k_st}, V{v, v_sb, v_sh, v_st}, PK{pre_k, pk_sb, pk_sh, pk_st};
+  dim3 grid(nchunks(seq_len), BH);
+  if (vec16)
+    prefill_scatter_kernel<true><<<grid, kScanThreads, 0, s>>>(pa, layer, seq_len, n_early, n_loc, nch, mv, K, V, PK,
+                                                               counts, first, okflag);
+  else
+    prefill_scatter_kernel<false><<<grid, kScanThreads, 0, s>>>(pa, layer, seq_len, n_early, n_loc, nch, mv, K, V, PK,
+                                                                counts, first, okflag);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream) {
+  if (!pool_ok(pool) || local_ptr < 0 || local_ptr >= pool->window) return WGKV_EINVAL;
+  PoolArgs pa{*pool};
+  promote_kernel<<<1, 1024, 0, as_stream(stream)>>>(pa, local_ptr);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                  const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
+                                  int64_t v_sb, int64_t v_sh, const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh,
+                                  int32_t* cache_seqlens, void* stream) {
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || insert_pos < 0 || insert_pos >= pool->window || !k_new ||
+      !v_new)
+    return WGKV_EINVAL;
+  if (((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+        reinterpret_cast<uintptr_t>(pre_k_new)) & 3) || ((k_sb | k_sh | v_sb | v_sh | pk_sb | pk_sh) & 1))
+    return WGKV_EINVAL;
+  PoolArgs pa{*pool};
+  const int BH = pool->batch * pool->kv_heads;
+  RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0}, PK{pre_k_new, pk_sb, pk_sh, 0};
+  decode_append_kernel<<<(BH + 7) / 8, 256, 0, as_stream(stream)>>>(pa, layer, insert_pos, cur_local_len, K, V, PK,
+                                                                    cache_seqlens);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}

@@ -11,4 +11,32 @@ from .decode import (  # noqa: F401
     flash_attn_with_kvcache_wrapper_triton_handle,
     paged_decode,
 )
+from .gate import GatingPredictor, GatingRMSNorm  # noqa: F401
+from .indices import generate_sparse_indices, sparse_indices_into  # noqa: F401
+from .layers import (  # noqa: F401
+    decode_wrapper,
+    migrate_local_kv_to_global,
+    prefill_wrapper,
+    refresh_local_is_global,
+    self_attn_forward_patch,
+    self_attn_forward_patch_inference,
+)
+from .pool import WgkvPool, init_pool  # noqa: F401
+from .prefill import sparse_attn_func, sparse_attn_func_wrapper  # noqa: F401
 from .runtime import check_errors  # noqa: F401
+
+
+def attach(attn, config=None):
+    """Install the WG-KV operator slots on an attention module, as
+    LlamaAttention.__init__ does (src/modeling_llama.py:240-250), pointing at
+    the CUDA implementations.  ``attn`` needs ``layer_idx``, ``head_dim``,
+    ``scaling`` and ``g_predictors`` (a :class:`GatingPredictor`)."""
+    if config is not None:
+        attn.config = config
+    attn.self_attn_forward_patch = self_attn_forward_patch
+    attn.prefill_wrapper = prefill_wrapper
+    attn.decode_wrapper = decode_wrapper
+    attn.prefill_kernel = sparse_attn_func_wrapper
+    attn.decode_kernel_handle = flash_attn_with_kvcache_wrapper_triton_handle
+    attn.decode_kernel_executor = lambda func: func()
+    return attn

@@ -1,0 +1,125 @@
+"""Write gate: GatingPredictor with the reference's parameters, CUDA forward.
+
+The module keeps the reference's sub-module names and shapes
+(src/modeling_layers.py:134-160: ``pre_key_norm`` / ``post_key_norm`` /
+``value_norm`` RMS norms, grouped 1x1 ``conv1`` and ``conv2``), so the
+published gate checkpoints (``model.layers.{i}.self_attn.g_predictors.*``)
+load with ``load_state_dict``.  ``forward`` runs the fast path
+(``:185-196``) as one sm_100a kernel (``wgkv_gate_scores``) and returns bf16
+scores of shape (B, Hk, L); :meth:`admit` writes the admission mask
+``scores > threshold`` straight into any uint8 tensor view (e.g. the
+cache's ``local_is_global`` slots) without materialising the scores.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ._lib import check, lib
+from .runtime import require_cuda, stream_ptr
+
+_SLOTS = ("pre_k", "post_k", "v")
+
+
+class GatingRMSNorm(nn.Module):
+    """Parameter holder with the reference's layout (``weight`` (D,), eps);
+    the normalisation itself runs inside the gate kernel."""
+
+    def __init__(self, hidden_size, eps=1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(hidden_size))
+        self.variance_epsilon = eps
+
+    def forward(self, hidden_states):  # pragma: no cover - the fused kernel is the product path
+        raise RuntimeError("GatingRMSNorm is applied inside wgkv_gate_scores")
+
+
+def _bf16(t):
+    return t.detach().to(torch.bfloat16).contiguous()
+
+
+def _strides4(t):
+    if t is None:
+        return 0, 0, 0, 0
+    assert t.dim() == 4 and t.stride(3) == 1, "gate inputs must be (B, Hk, L, D) with a contiguous last axis"
+    return t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)
+
+
+class GatingPredictor(nn.Module):
+    def __init__(self, head_dim, num_kv_heads, g_inputs, g_act_fn, g_expand, g_epsilon, g_rms, g_fast_path=True):
+        super().__init__()
+        self.g_inputs = list(g_inputs)
+        self.g_epsilon = g_epsilon
+        self.g_fast_path = g_fast_path
+        self.head_dim = head_dim
+        self.num_kv_heads = num_kv_heads
+        self.input_dim = head_dim * len(self.g_inputs)
+        self.inner_dim = int(head_dim * g_expand)
+        self.g_rms = g_rms
+        self.act = 1 if g_act_fn == "silu" else 0
+        self.pre_key_norm = GatingRMSNorm(head_dim) if g_rms and "pre_k" in self.g_inputs else nn.Identity()
+        self.post_key_norm = GatingRMSNorm(head_dim) if g_rms and "post_k" in self.g_inputs else nn.Identity()
+        self.value_norm = GatingRMSNorm(head_dim) if g_rms and "v" in self.g_inputs else nn.Identity()
+        self.conv1 = nn.Conv1d(num_kv_heads * self.input_dim, num_kv_heads * self.inner_dim, kernel_size=1,
+                               groups=num_kv_heads)
+        self.conv2 = nn.Conv1d(num_kv_heads * self.inner_dim, num_kv_heads, kernel_size=1, groups=num_kv_heads)
+        self.input_mask = sum(1 << i for i, s in enumerate(_SLOTS) if s in self.g_inputs)
+        # the kernel concatenates inputs in slot order; the reference concatenates in that order too (:173-183)
+
+    def reset_parameters(self):
+        for norm in (self.pre_key_norm, self.post_key_norm, self.value_norm):
+            if isinstance(norm, GatingRMSNorm):
+                nn.init.ones_(norm.weight)
+        self.conv1.reset_parameters()
+        self.conv2.reset_parameters()
+
+    def _norm_weights(self, device):
+        if not self.g_rms:
+            return None
+        rows = []
+        for mod in (self.pre_key_norm, self.post_key_norm, self.value_norm):
+            rows.append(mod.weight if isinstance(mod, GatingRMSNorm) else torch.ones(self.head_dim, device=device))
+        return _bf16(torch.stack([r.to(device) for r in rows]))
+
+    def _eps(self):
+        for mod in (self.pre_key_norm, self.post_key_norm, self.value_norm):
+            if isinstance(mod, GatingRMSNorm):
+                return float(mod.variance_epsilon)
+        return 1e-6
+
+    def _launch(self, pre_key, post_key, value, threshold, scores, mask):
+        ref = next(t for t in (pre_key, post_key, value) if t is not None)
+        require_cuda(ref, "gate input")
+        B, Hk, L, D = ref.shape
+        assert Hk == self.num_kv_heads and D == self.head_dim
+        ins = {"pre_k": pre_key, "post_k": post_key, "v": value}
+        for s in self.g_inputs:
+            assert ins[s] is not None and ins[s].dtype == torch.bfloat16, f"gate input {s} must be bf16"
+        w1 = _bf16(self.conv1.weight)  # (Hk*inner, I, 1) == (Hk, inner, I)
+        b1 = _bf16(self.conv1.bias)
+        w2 = _bf16(self.conv2.weight)  # (Hk, inner, 1)
+        b2 = _bf16(self.conv2.bias)
+        nw = self._norm_weights(ref.device)
+        pk = _strides4(pre_key if "pre_k" in self.g_inputs else None)
+        kk = _strides4(post_key if "post_k" in self.g_inputs else None)
+        vv = _strides4(value if "v" in self.g_inputs else None)
+        sp = (scores.data_ptr(), scores.stride(0), scores.stride(1), scores.stride(2)) if scores is not None else (0, 0, 0, 0)
+        mp = (mask.data_ptr(), mask.stride(0), mask.stride(1), mask.stride(2)) if mask is not None else (0, 0, 0, 0)
+        st = lib.wgkv_gate_scores(*pk, *kk, *vv, B, Hk, L, D, self.input_mask, w1.data_ptr(), b1.data_ptr(),
+                                  w2.data_ptr(), b2.data_ptr(), nw.data_ptr() if nw is not None else None,
+                                  self._eps(), self.inner_dim, self.act, float(threshold), *sp, *mp,
+                                  stream_ptr(ref.device))
+        check(st, "wgkv_gate_scores")
+
+    def forward(self, pre_key, post_key, value):
+        """g_scores (B, Hk, L) bf16 (GatingPredictor.forward fast path, :170-196)."""
+        ref = post_key if post_key is not None else (pre_key if pre_key is not None else value)
+        B, Hk, L, _ = ref.shape
+        scores = torch.empty(B, Hk, L, dtype=torch.bfloat16, device=ref.device)
+        self._launch(pre_key, post_key, value, 0.0, scores, None)
+        return scores
+
+    def admit(self, pre_key, post_key, value, threshold, mask, scores=None):
+        """Write ``gate(x) > threshold`` (uint8) into ``mask`` (any (B, Hk, L) view); optionally the scores."""
+        self._launch(pre_key, post_key, value, threshold, scores, mask)
+        return mask

@@ -1,0 +1,198 @@
+"""The WG-KV attention patch on the CUDA kernels: reference-named drop-ins.
+
+Mirrors the operator surface the patched Llama/Qwen3 attention layers call
+(src/modeling_llama.py:240-250, :273-287; src/modeling_layers.py):
+
+* ``self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value,
+  input_shape, query_states, pre_key, key_states, value_states)`` (:1534)
+* ``self_attn_forward_patch_inference`` (:1452), ``prefill_wrapper`` (:1183),
+  ``decode_wrapper`` (:1379), ``migrate_local_kv_to_global`` (:674),
+  ``refresh_local_is_global`` (:1169)
+
+``self`` is the attention module (``layer_idx``, ``config``, ``head_dim``,
+``scaling``, ``g_predictors`` and the kernel slots); ``past_key_value`` is any
+attribute holder (the HF cache object), which gets the pool attributes of
+:func:`wgkv.pool.init_pool`.  Differences from the reference, all on the
+host side: batch > 1 is accepted (the pool has a batch axis); no step
+synchronises the host (page allocation, compaction and the decode schedule
+run on the device); capacity violations are reported through the device
+error word (``wgkv.check_errors()``), not an immediate assert.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, lib
+from .indices import sparse_indices_into
+from .pool import init_pool, pool_ref
+from .runtime import stream_ptr, workspace
+
+
+def _cfg(self):
+    return self.config
+
+
+def _maybe_init(self, past_key_value, batch_size, key_states):
+    c = _cfg(self)
+    if not getattr(past_key_value, "gated_kv_initialized", False):
+        assert self.layer_idx == 0, "the pool is created by layer 0's prefill"
+        init_pool(past_key_value, layers=c.num_hidden_layers, batch=batch_size, kv_heads=c.num_key_value_heads,
+                  head_dim=self.head_dim, window=c.local_window_size, page=c.block_size,
+                  max_total_tokens=c.max_total_tokens, max_tokens_per_head=c.max_tokens_per_head,
+                  device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)))
+    elif self.layer_idx == 0:
+        raise AssertionError("prefill on an initialised cache (the reference asserts the same, :1197)")
+
+
+def _s4(t):
+    return (t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)) if t is not None else (None, 0, 0, 0)
+
+
+def prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, batch_size, q_seq_len,
+                    device, g_mask, local_blocks_per_head):
+    """Ring fill + admission compaction + sparse indices + sparse prefill (:1183-1376).
+
+    q (B, Hq, L, D), pre_key/key/value (B, Hk, L, D), g_mask (B, Hk, L) bool/uint8.
+    Returns (B, L, Hq, D)."""
+    c = _cfg(self)
+    _maybe_init(self, past_key_value, batch_size, key_states)
+    if g_mask.dtype == torch.bool:
+        g_mask = g_mask.view(torch.uint8)
+    W = c.local_window_size
+    L = q_seq_len
+    defer = past_key_value.local_pre_key is not None
+    nbytes = int(lib.wgkv_prefill_admit_workspace_size(batch_size, c.num_key_value_heads, max(L - W, 0)))
+    ws = workspace(device, "prefill_admit", nbytes)
+    st = lib.wgkv_prefill_admit(pool_ref(past_key_value), self.layer_idx, L, *_s4(key_states), *_s4(value_states),
+                                *_s4(pre_key if defer else None), *_s4(g_mask), ws.data_ptr(), ws.numel(),
+                                stream_ptr(device))
+    check(st, "wgkv_prefill_admit")
+    past_key_value.local_length = min(L, W)
+    bc, bo, cc, ci = sparse_indices_into(g_mask, W, L, 64)
+    return self.prefill_kernel(query_states.transpose(1, 2), key_states.transpose(1, 2),
+                               value_states.transpose(1, 2), bc, bo, cc, ci, softmax_scale=self.scaling,
+                               causal=True, return_softmax_lse=False)
+
+
+def migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head):
+    """Lazy promotion of every (layer, b, h) ring slot at local_ptr (:674-763), one launch."""
+    st = lib.wgkv_promote(pool_ref(past_key_value), int(past_key_value.local_ptr), stream_ptr(device))
+    check(st, "wgkv_promote")
+
+
+def refresh_local_is_global(self, past_key_value, device):
+    """Deferred gating: re-score this layer's whole ring (:1169-1180)."""
+    c = _cfg(self)
+    l = self.layer_idx
+    B, Hk, W, D = past_key_value.wgkv_batch, c.num_key_value_heads, c.local_window_size, self.head_dim
+    n_ring = c.num_hidden_layers * B * Hk * W
+    ring_k = past_key_value.block_pool_k[:n_ring].view(c.num_hidden_layers, B, Hk, W, D)[l]
+    ring_v = past_key_value.block_pool_v[:n_ring].view(c.num_hidden_layers, B, Hk, W, D)[l]
+    self.g_predictors.admit(past_key_value.local_pre_key[l], ring_k, ring_v, c.g_threshold,
+                            past_key_value.local_is_global[l])
+
+
+def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, g_mask,
+                   local_blocks_per_head):
+    """Ring append + (deferred) admission + ragged paged attention for one token (:1379-1449).
+
+    ``g_mask`` (B, Hk, 1): the new token's admission bit, or None when it was
+    already written into ``local_is_global`` by the fused gate (or deferred)."""
+    c = _cfg(self)
+    W = c.local_window_size
+    l = self.layer_idx
+    if past_key_value.local_length < W:
+        insert_pos = past_key_value.local_length
+        cur = past_key_value.local_length + 1
+    else:
+        insert_pos = past_key_value.local_ptr
+        cur = W
+    defer = past_key_value.local_pre_key is not None
+    k1 = key_states[:, :, 0]
+    v1 = value_states[:, :, 0]
+    p1 = pre_key[:, :, 0] if (defer and pre_key is not None) else None
+    st = lib.wgkv_decode_append(pool_ref(past_key_value), l, insert_pos, cur, k1.data_ptr(), k1.stride(0),
+                                k1.stride(1), v1.data_ptr(), v1.stride(0), v1.stride(1),
+                                p1.data_ptr() if p1 is not None else None, p1.stride(0) if p1 is not None else 0,
+                                p1.stride(1) if p1 is not None else 0, past_key_value.cache_seqlens.data_ptr(),
+                                stream_ptr(device))
+    check(st, "wgkv_decode_append")
+    if g_mask is not None:
+        past_key_value.local_is_global[l, :, :, insert_pos] = g_mask[:, :, 0].to(torch.uint8)
+    elif defer and insert_pos == W - 1:
+        refresh_local_is_global(self, past_key_value, device)
+    if l == c.num_hidden_layers - 1:
+        if past_key_value.local_length < W:
+            past_key_value.local_length = cur
+        else:
+            past_key_value.local_ptr = (past_key_value.local_ptr + 1) % W
+    T = c.block_size
+    k_cache = past_key_value.block_pool_k.view(past_key_value.total_blocks, T, self.head_dim)
+    v_cache = past_key_value.block_pool_v.view(past_key_value.total_blocks, T, self.head_dim)
+    handle = self.decode_kernel_handle(query_states.transpose(1, 2), k_cache, v_cache, past_key_value.cache_seqlens,
+                                       past_key_value.block_table[l], self.scaling)
+    return self.decode_kernel_executor(handle)
+
+
+def self_attn_forward_patch_inference(self, past_key_value, input_shape, query_states, pre_key, key_states,
+                                      value_states, g_scores, g_mask=None):
+    """:1452-1509.  Either ``g_scores`` (thresholded here, as the reference
+    does) or a precomputed uint8 ``g_mask`` may be given; with neither on a
+    decode step the new token's bit is expected in ``local_is_global``
+    already (fused gate) or deferred."""
+    c = _cfg(self)
+    batch_size, q_seq_len = input_shape
+    device = query_states.device
+    is_prefilling = q_seq_len > 1
+    if g_mask is None and g_scores is not None:
+        g_mask = (g_scores > c.g_threshold).to(torch.uint8)
+    assert c.local_window_size % c.block_size == 0
+    local_blocks_per_head = c.local_window_size // c.block_size
+    if (not is_prefilling) and self.layer_idx == 0 and past_key_value.local_length == c.local_window_size:
+        migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
+    if is_prefilling:
+        return self.prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states,
+                                    batch_size, q_seq_len, device, g_mask, local_blocks_per_head)
+    return self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, g_mask,
+                               local_blocks_per_head)
+
+
+def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, input_shape, query_states, pre_key,
+                            key_states, value_states):
+    """:1534-1629, inference mode (gating_mode 3) only: training and the
+    comparison baselines are outside this library.
+
+    Prefill: the gate writes the admission mask (one kernel).  Decode without
+    deferral: the gate writes the new token's bit straight into the cache's
+    ``local_is_global`` ring slot (after the layer-0 promotion has read the
+    old bit), so no scores tensor is materialised."""
+    if gating_mode != 3:
+        raise NotImplementedError("only WG-KV inference (gating_mode=3) is implemented on the CUDA path")
+    assert attention_mask is None
+    assert past_key_value is not None
+    c = _cfg(self)
+    batch_size, q_len = input_shape
+    kv_seq_len = key_states.size(2)
+    device = query_states.device
+    if kv_seq_len > 1:
+        B, Hk, L, _ = key_states.shape
+        g_mask = torch.empty(B, Hk, L, dtype=torch.uint8, device=device)
+        self.g_predictors.admit(pre_key, key_states, value_states, c.g_threshold, g_mask)
+        out = self_attn_forward_patch_inference(self, past_key_value, input_shape, query_states, pre_key,
+                                                key_states, value_states, None, g_mask=g_mask)
+        return out, None, None
+    if getattr(c, "g_defer", False):
+        out = self_attn_forward_patch_inference(self, past_key_value, input_shape, query_states, pre_key,
+                                                key_states, value_states, None)
+        return out, None, None
+    W = c.local_window_size
+    local_blocks_per_head = W // c.block_size
+    l = self.layer_idx
+    if l == 0 and past_key_value.local_length == W:
+        migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
+    insert_pos = past_key_value.local_length if past_key_value.local_length < W else past_key_value.local_ptr
+    self.g_predictors.admit(pre_key, key_states, value_states, c.g_threshold,
+                            past_key_value.local_is_global[l, :, :, insert_pos:insert_pos + 1])
+    out = self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, None,
+                              local_blocks_per_head)
+    return out, None, None
