@@ -1,0 +1,465 @@
+"""Benchmark of the WG-KV admission hot path on B200.
+
+Default workload: Llama-3.1-8B-shaped decode, 32 layers,
+batch 16, 128K-token context per sequence, 32 query / 8 KV heads, d=128,
+bf16, a 4096-token local ring, page size 16, per-(layer, sequence, head)
+global lengths from admit rates ~ Beta(2, 8).  One step = one decode token
+for every sequence through all 32 layers of the hot path: write gate on the
+new key, lazy promotion (layer 0), ring append, ragged paged attention --
+called through the reference-named patch ``self_attn_forward_patch``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Under torchrun (N > 1) every rank runs its own batch-16 workload on its own
+GPU (weak scaling: sequences are independent, no collective on the data
+path); the step time is the max over ranks.  ``--impl reference`` times the
+reference algorithm's CPU restatement (the test oracle) on the host cores.
+Inputs are synthetic (seeded N(0,1) bf16, random-init gate weights); the
+cache (~62 GB) is far larger than L2, so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "wg-kv_b200"))
+
+CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=16, ctx=131072, q_heads=32, kv_heads=8, head_dim=128,
+           window=4096, page=16, admit="Beta(2,8)", gate="pre_k->64->1 GELU sigmoid", threshold=0.5)
+METRIC = "decode tok/s @128K ragged cache (Llama-8B shape, B=16, 32 layers)"
+
+
+def peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# synthetic decode state
+# ----------------------------------------------------------------------------
+
+def draw_lengths(seed, Ly, B, Hk, ctx, W):
+    rng = np.random.default_rng(seed)
+    rate = rng.beta(2, 8, (Ly, B, Hk))
+    glen = np.round(rate * (ctx - W)).astype(np.int64)
+    return rate, glen
+
+
+def build_state(dev, steps_total, seed=2):
+    import torch
+    import wgkv
+    Ly, B, Hk, Hq, D = CFG["layers"], CFG["batch"], CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"]
+    W, T, ctx = CFG["window"], CFG["page"], CFG["ctx"]
+    rate, glen = draw_lengths(seed, Ly, B, Hk, ctx, W)
+    gpages = (glen + T - 1) // T
+    ring_pages = Ly * B * Hk * (W // T)
+    grow = (steps_total + T - 1) // T + 1  # pages a head may gain during the run
+    total_blocks = int(ring_pages + gpages.sum() + Ly * B * Hk * grow + 1)
+    max_tokens_per_head = int(W + glen.max() + steps_total + T)
+    cache = SimpleNamespace()
+    wgkv.init_pool(cache, layers=Ly, batch=B, kv_heads=Hk, head_dim=D, window=W, page=T,
+                   max_total_tokens=total_blocks * T, max_tokens_per_head=max_tokens_per_head, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    rows = cache.block_pool_k.shape[0]
+    step = 1 << 26
+    for t in (cache.block_pool_k, cache.block_pool_v):
+        for r0 in range(0, rows, step):
+            r1 = min(rows, r0 + step)
+            t[r0:r1].normal_(generator=g)
+    # global pages: a random permutation of the pool after the ring pages (as utils/benchmark_decode.py:72-77)
+    n_g = int(gpages.sum())
+    perm = torch.randperm(n_g, generator=torch.Generator().manual_seed(seed), dtype=torch.int64).to(torch.int32)
+    perm += ring_pages
+    table = cache.block_table.view(Ly * B * Hk, -1)
+    lp = W // T
+    flat_pages = gpages.reshape(-1)
+    off = 0
+    host_rows = table[:, lp:].cpu()
+    for i, n in enumerate(flat_pages):
+        n = int(n)
+        host_rows[i, :n] = perm[off:off + n]
+        off += n
+    table[:, lp:].copy_(host_rows.to(dev))
+    cache.global_lengths.copy_(torch.from_numpy(glen.astype(np.int32)).to(dev))
+    lig = torch.from_numpy((np.random.default_rng(seed + 1).random((Ly, B, Hk, W)) < rate[..., None]).astype(np.uint8))
+    cache.local_is_global.copy_(lig.to(dev))
+    cache.next_free_block.fill_(ring_pages + n_g)
+    cache.local_length = W
+    cache.local_ptr = 0
+    return cache, rate, glen
+
+
+def build_layers(dev, rate, seed=3):
+    import torch
+    import torch.nn.functional as F
+    import wgkv
+    Ly, Hk, D = CFG["layers"], CFG["kv_heads"], CFG["head_dim"]
+    cfg = SimpleNamespace(num_hidden_layers=Ly, num_key_value_heads=Hk, num_attention_heads=CFG["q_heads"],
+                          head_dim=D, block_size=CFG["page"], local_window_size=CFG["window"], g_defer=False,
+                          g_threshold=CFG["threshold"], max_total_tokens=None, max_tokens_per_head=None)
+    torch.manual_seed(seed)
+    layers = []
+    x = torch.randn(4096, D, device=dev)
+    for l in range(Ly):
+        gp = wgkv.GatingPredictor(D, Hk, ["pre_k"], "gelu", 0.5, 1e-3, False, True).to(dev, torch.bfloat16)
+        # bias per head so that P(score > 0.5) ~ the head's admit rate (calibrated on N(0,1) keys)
+        with torch.no_grad():
+            w1 = gp.conv1.weight.float().view(Hk, -1, D)
+            b1 = gp.conv1.bias.float().view(Hk, -1)
+            w2 = gp.conv2.weight.float().view(Hk, -1)
+            hdn = F.gelu(torch.einsum("td,hjd->htj", x, w1) + b1[:, None, :])
+            logit = torch.einsum("htj,hj->ht", hdn, w2)
+            r = torch.from_numpy(rate[l].mean(axis=0)).to(dev).float()
+            b2 = -torch.stack([torch.quantile(logit[h], 1 - r[h]) for h in range(Hk)])
+            gp.conv2.bias.copy_(b2.to(torch.bfloat16))
+        a = SimpleNamespace(layer_idx=l, head_dim=D, scaling=D ** -0.5, g_predictors=gp)
+        wgkv.attach(a, cfg)
+        layers.append(a)
+    return layers
+
+
+def algorithmic_bytes(cache, glen_now):
+    """Bytes one decode step must move (K/V of every live token, q/o, page ids, append, gate input)."""
+    Ly, B, Hk, Hq, D, W, T = (CFG[k] for k in ("layers", "batch", "kv_heads", "q_heads", "head_dim", "window", "page"))
+    seqlen = W + glen_now
+    attn = int(seqlen.sum()) * D * 2 * 2
+    pages = int(((seqlen + T - 1) // T).sum()) * 4
+    qo = Ly * B * Hq * D * 2 * 2
+    append = Ly * B * Hk * D * 2 * 2 * 2  # read new k/v, write ring
+    gate = Ly * B * Hk * D * 2
+    return attn + pages + qo + append + gate, attn + pages + qo
+
+
+# ----------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        lines = open(self.f.name).read().strip().splitlines()
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in lines:
+            c = [x.strip() for x in ln.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1].split()[0]))
+                mx = float(c[2].split()[0])
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# CPU arms (the oracle restatement of the reference algorithm)
+# ----------------------------------------------------------------------------
+
+def cpu_sample_step(seed=5):
+    """One bounded CPU sample: one sequence x one layer of the step (gate on
+    the new key, ring append, promotion, paged attention over the 8 heads at
+    the workload's length distribution).  Returns (callable, description)."""
+    from oracle import wgkv_oracle as O
+    Hk, Hq, D, W, T, ctx = (CFG[k] for k in ("kv_heads", "q_heads", "head_dim", "window", "page", "ctx"))
+    rate, glen = draw_lengths(2, 1, 1, Hk, ctx, W)
+    st = O.PoolState(layers=1, batch=1, kv_heads=Hk, head_dim=D, window=W, page=T,
+                     max_total_tokens=int((Hk * W + glen.sum() + Hk * 64) + 64) * 1,
+                     max_tokens_per_head=int(W + glen.max() + 256), defer=False)
+    rng = np.random.default_rng(seed)
+    st.k[:] = rng.standard_normal(st.k.shape, dtype=np.float32)
+    st.v[:] = rng.standard_normal(st.v.shape, dtype=np.float32)
+    nxt = st.next_free_block
+    for h in range(Hk):
+        n = int(glen[0, 0, h])
+        np_ = (n + T - 1) // T
+        st.block_table[0, 0, h, W // T:W // T + np_] = np.arange(nxt, nxt + np_)
+        nxt += np_
+        st.global_lengths[0, 0, h] = n
+    st.next_free_block = nxt
+    st.local_length = W
+    st.local_is_global[:] = rng.random(st.local_is_global.shape) < 0.2
+    inner = 64
+    p = O.GateParams(w1=O.bf16(rng.uniform(-0.09, 0.09, (Hk, inner, D)).astype(np.float32)),
+                     b1=O.bf16(rng.uniform(-0.09, 0.09, (Hk, inner)).astype(np.float32)),
+                     w2=O.bf16(rng.uniform(-0.12, 0.12, (Hk, inner)).astype(np.float32)), b2=np.zeros(Hk, np.float32))
+    q = O.randn_bf16(rng, (1, 1, Hq, D))
+    kn, vn, pk = (O.randn_bf16(rng, (1, Hk, 1, D)) for _ in range(3))
+
+    def run():
+        s = O.gate_scores(p, pre_key=pk)
+        st.promote()
+        cur = st.append_layer(0, kn[:, :, 0], vn[:, :, 0], O.admission_mask(s, CFG["threshold"])[:, :, 0])
+        sl, bt = st.decode_tables(0, cur)
+        kc, vc = st.paged_views()
+        O.paged_decode(q, kc, vc, sl, bt, D ** -0.5)
+        st.local_length = W  # keep the ring full for the next sample
+    desc = (f"1 sequence x 1 layer of the decode step (8 KV heads, {int((W + glen).sum())} cached tokens, "
+            f"gate+promote+append+attention), numpy oracle; tok/s = 1 / (t_sample x 32 layers)")
+    return run, desc
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def time_cpu(budget_s=15.0, min_reps=2, max_reps=50):
+    run, desc = cpu_sample_step()
+    run()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < min_reps or (time.perf_counter() - t0 < budget_s and reps < max_reps):
+        run()
+        reps += 1
+    t = (time.perf_counter() - t0) / reps
+    return 1.0 / (t * CFG["layers"]), desc + f"; {reps} samples of {t * 1e3:.1f} ms"
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    run, desc = cpu_sample_step()
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    t = (time.perf_counter() - t0) / args.steps
+    val = 1.0 / (t * CFG["layers"])
+    cores = blas_threads()
+    line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "C2 decode (one step sample: 1 sequence x 1 layer)", **CFG},
+            "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def gpu_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import wgkv
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    Ly, B, Hk, Hq, D = CFG["layers"], CFG["batch"], CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"]
+    steps_total = args.warmup + 2 * args.steps + 8
+    cache, rate, glen0 = build_state(dev, steps_total, seed=2 + 1000 * rank)
+    layers = build_layers(dev, rate, seed=3 + 1000 * rank)
+    NI = 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    # per-step inputs, laid out as a projection would produce them: (B, H, 1, D)
+    per_layer = Hq + 3 * Hk
+    inputs = torch.randn(NI, Ly, B, per_layer, 1, D, generator=g, device=dev).to(torch.bfloat16)
+
+    def split(x):
+        return x[:, :Hq], x[:, Hq:Hq + Hk], x[:, Hq + Hk:Hq + 2 * Hk], x[:, Hq + 2 * Hk:]
+
+    outbuf = torch.empty(Ly, B, 1, Hq, D, dtype=torch.bfloat16, device=dev)
+
+    def step(inp):
+        for l in range(Ly):
+            q, k, v, pk = split(inp[l])
+            a = layers[l]
+            o, _, _ = a.self_attn_forward_patch(a, 3, None, cache, (B, 1), q, pk, k, v)
+            outbuf[l].copy_(o)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for s in range(args.warmup):
+        step(inputs[s % NI])
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    glen_start = cache.global_lengths.cpu().numpy().astype(np.int64)
+
+    # ---- device-resident timed region ----
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    l0 = wgkv.lib.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(args.steps):
+        step(inputs[s % NI])
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = wgkv.lib.launches - l0
+    ms = e0.elapsed_time(e1)
+    clocks = clk.stop() if clk else None
+    wgkv.check_errors()
+    glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * B * args.steps / (ms / 1e3)
+    bytes_step, _ = algorithmic_bytes(cache, (glen_start + glen_end) / 2.0)
+
+    # ---- end-to-end through the public API with host buffers ----
+    host_in = torch.empty(NI, *inputs.shape[1:], dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(inputs)
+    dev_in = torch.empty_like(inputs[0])
+    host_out = torch.empty(outbuf.shape, dtype=torch.bfloat16, pin_memory=True)
+    e_steps = max(1, min(args.steps, 64))
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for s in range(e_steps):
+        dev_in.copy_(host_in[s % NI], non_blocking=True)
+        step(dev_in)
+        host_out.copy_(outbuf, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    barrier()
+    te = torch.tensor([e2.elapsed_time(e3)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = world * B * e_steps / (float(te.item()) / 1e3)
+    wgkv.check_errors()
+
+    # ---- roofline of the dominant kernel (paged decode), timed alone ----
+    T = CFG["page"]
+    W = CFG["window"]
+    kc = cache.block_pool_k.view(cache.total_blocks, T, D)
+    vc = cache.block_pool_v.view(cache.total_blocks, T, D)
+    gl = cache.global_lengths
+    seq_l = [(gl[l] + W).to(torch.int32).contiguous() for l in range(Ly)]
+    qd = inputs[0, :, :, :Hq].transpose(2, 3)  # (Ly, B, 1, Hq, D) view
+    od = torch.empty(B, 1, Hq, D, dtype=torch.bfloat16, device=dev)
+    reps = 3
+    for l in range(Ly):
+        wgkv.paged_decode(qd[l].contiguous(), kc, vc, seq_l[l], cache.block_table[l], D ** -0.5, out=od)
+    qs = [qd[l].contiguous() for l in range(Ly)]
+    torch.cuda.synchronize()
+    e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e4.record()
+    for _ in range(reps):
+        for l in range(Ly):
+            wgkv.paged_decode(qs[l], kc, vc, seq_l[l], cache.block_table[l], D ** -0.5, out=od)
+    e5.record()
+    torch.cuda.synchronize()
+    per_launch_ms = e4.elapsed_time(e5) / (reps * Ly)
+    glen_now = cache.global_lengths.cpu().numpy().astype(np.int64)
+    sl = W + glen_now
+    kbytes = (int(sl.sum()) * D * 2 * 2 + int(((sl + T - 1) // T).sum()) * 4 + Ly * B * Hq * D * 2 * 2) / Ly
+    achieved = kbytes / (per_launch_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    prof = os.path.join(HERE, "profiles", "paged_decode_traffic.json")
+    if os.path.exists(prof):
+        try:
+            d = json.load(open(prof))
+            traffic = float(d["dram_bytes_per_token"]) * (int(sl.sum()) / Ly)
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        cpu_val, cpu_desc = (None, None)
+        if world == 1:
+            cpu_val, cpu_desc = time_cpu()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2 decode: Llama-3.1-8B shape, B=16/GPU, 128K ctx, W=4096, T=16, Beta(2,8) admit",
+                       "l2": "inputs larger than L2 (~62 GB cache), no flush", "parallelism": f"dp{world} (sequences)",
+                       **CFG},
+            "hbm_gbs_step": bytes_step / (ms_step / 1e3) / 1e9,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(inputs[0].numel() * 2),
+                    "d2h_bytes_per_step": int(outbuf.numel() * 2)},
+            "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                         "bytes_per_launch": kbytes, "ms_per_launch": per_launch_ms},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        if cpu_val is not None:
+            line["cpu_baseline"] = {"value": cpu_val, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+                                    "sample": cpu_desc}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        gpu_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -59,6 +59,7 @@ class _Lib:
     def __init__(self):
         self._lib = None
         self.decls = parse_header()
+        self.launches = 0
 
     def load(self):
         if self._lib is None:
@@ -74,8 +75,21 @@ class _Lib:
 
     def __getattr__(self, name):
         if name.startswith("wgkv_"):
-            return getattr(self.load(), name)
+            fn = getattr(self.load(), name)
+            n = KERNELS_PER_CALL.get(name)
+            if n is None:
+                return fn
+
+            def counted(*args, _fn=fn, _n=n):
+                self.launches += _n
+                return _fn(*args)
+            return counted
         raise AttributeError(name)
+
+
+# kernels each compute entry point launches (for the benchmark's launch count)
+KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_append": 1, "wgkv_promote": 1,
+                    "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1}
 
 
 lib = _Lib()
