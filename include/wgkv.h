@@ -214,6 +214,34 @@ WGKV_API int wgkv_paged_decode(const uint16_t* q, const uint16_t* k_cache, const
                       int batch, int num_q_heads, int num_kv_heads, int head_dim, float softmax_scale, uint16_t* out,
                       void* workspace, size_t workspace_bytes, int* err, void* stream);
 
+/*
+ * Paged decode without any device allocation -- no counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc on the decode path: a serving engine
+ * that owns the whole device-memory budget and hands kernels only its own
+ * buffers, or a plugin invoked while its host framework captures a stream.
+ * Same inputs, outputs and results as wgkv_paged_decode; the split-K scratch
+ * (per-head counters + partial softmax states) lives in one static device
+ * array of WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES inside libwgkv.so, which
+ * every GPU that loads the library keeps until the process exits.
+ *   - Needs (batch*kv_heads*4 rounded up to 256) + (batch*kv_heads + SMs) *
+ *     (q_heads/kv_heads) * (head_dim + 2) * 4 bytes; larger problems return
+ *     WGKV_ENOSPC and launch nothing (e.g. batch 64 x 8 kv heads x 4 groups x
+ *     d 128 needs ~1.4 MiB and fits).
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Each call clears the counters with cudaMemsetAsync on `stream`; it calls
+ *     no cudaMalloc / cudaFree.  All calls share the one array, so calls that
+ *     can overlap on the GPU (different streams without ordering) race: order them.
+ */
+#define WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES (4u << 20)
+WGKV_API int wgkv_paged_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                       int64_t num_pages, int page_size, const int32_t* cache_seqlens,
+                                       const int32_t* block_table, int64_t table_stride, int batch, int num_q_heads,
+                                       int num_kv_heads, int head_dim, float softmax_scale, uint16_t* out, int* err,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,8 @@
 //   with P rounded to bf16 before PV, as the reference kernel does (:930).
 // * A head covered by several CTAs is merged by the last CTA to finish it
 //   (per-head atomic counter, self-resetting); no spin waits.
+#include <mutex>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -478,4 +480,47 @@ extern "C" int wgkv_paged_decode(const uint16_t* q, const uint16_t* k_cache, con
     default:
       return WGKV_EINVAL;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: split-K scratch in a file-scope device array.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_decode_scratch[WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {nullptr};
+
+// Device address of g_decode_scratch on the current device (resolved once per
+// device; the symbol's host-side name is not a device address).
+void* static_scratch(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess) return nullptr;
+    g_scratch_addr[dev] = p;
+  }
+  return g_scratch_addr[dev];
+}
+}  // namespace
+
+extern "C" int wgkv_paged_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                         int64_t num_pages, int page_size, const int32_t* cache_seqlens,
+                                         const int32_t* block_table, int64_t table_stride, int batch,
+                                         int num_q_heads, int num_kv_heads, int head_dim, float softmax_scale,
+                                         uint16_t* out, int* err, void* stream) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
+  const size_t need = wgkv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim);
+  if (need > WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES) return WGKV_ENOSPC;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return WGKV_ECUDA;
+  void* scratch = static_scratch(dev);
+  if (!scratch) return WGKV_ECUDA;
+  // the per-head counters must start at zero (the array keeps the last call's contents)
+  const size_t counter_bytes = size_t(batch) * num_kv_heads * 4;
+  if (cudaMemsetAsync(scratch, 0, counter_bytes, wgkv::as_stream(stream)) != cudaSuccess) return WGKV_ECUDA;
+  return wgkv_paged_decode(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table, table_stride, batch,
+                           num_q_heads, num_kv_heads, head_dim, softmax_scale, out, scratch,
+                           WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES, err, stream);
 }
