@@ -299,28 +299,35 @@ def gpu_arm(args, rank, world, local_rank):
     NI = 4
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
-    # per-step inputs, laid out as a projection would produce them: (B, H, 1, D)
+    # per-step inputs laid out as the q/k/v projections produce them, (B, 1, H, D), viewed (B, H, 1, D)
     per_layer = Hq + 3 * Hk
-    inputs = torch.randn(NI, Ly, B, per_layer, 1, D, generator=g, device=dev).to(torch.bfloat16)
-
-    def split(x):
-        return x[:, :Hq], x[:, Hq:Hq + Hk], x[:, Hq + Hk:Hq + 2 * Hk], x[:, Hq + 2 * Hk:]
+    inputs = torch.randn(NI, Ly, B, 1, per_layer, D, generator=g, device=dev).to(torch.bfloat16)
+    qbuf = inputs[:, :, :, :, :Hq].contiguous()
 
     outbuf = torch.empty(Ly, B, 1, Hq, D, dtype=torch.bfloat16, device=dev)
+    outs = [None] * Ly
 
-    def step(inp):
+    def step(s, inp=None, qin=None):
         for l in range(Ly):
-            q, k, v, pk = split(inp[l])
+            if inp is None:
+                x = inputs[s % NI, l]
+                q = qbuf[s % NI, l].transpose(1, 2)
+            else:
+                x = inp[l]
+                q = qin[l].transpose(1, 2)
+            k = x[:, :, Hq:Hq + Hk].transpose(1, 2)
+            v = x[:, :, Hq + Hk:Hq + 2 * Hk].transpose(1, 2)
+            pk = x[:, :, Hq + 2 * Hk:].transpose(1, 2)
             a = layers[l]
             o, _, _ = a.self_attn_forward_patch(a, 3, None, cache, (B, 1), q, pk, k, v)
-            outbuf[l].copy_(o)
+            outs[l] = o
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     for s in range(args.warmup):
-        step(inputs[s % NI])
+        step(s)
     torch.cuda.synchronize()
     wgkv.check_errors()
     glen_start = cache.global_lengths.cpu().numpy().astype(np.int64)
@@ -331,10 +338,12 @@ def gpu_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     l0 = wgkv.lib.launches
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("wgkv_timed")
     e0.record()
     for s in range(args.steps):
-        step(inputs[s % NI])
+        step(s)
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     launches = wgkv.lib.launches - l0
@@ -353,7 +362,10 @@ def gpu_arm(args, rank, world, local_rank):
     # ---- end-to-end through the public API with host buffers ----
     host_in = torch.empty(NI, *inputs.shape[1:], dtype=torch.bfloat16, pin_memory=True)
     host_in.copy_(inputs)
+    host_q = torch.empty(NI, *qbuf.shape[1:], dtype=torch.bfloat16, pin_memory=True)
+    host_q.copy_(qbuf)
     dev_in = torch.empty_like(inputs[0])
+    dev_q = torch.empty_like(qbuf[0])
     host_out = torch.empty(outbuf.shape, dtype=torch.bfloat16, pin_memory=True)
     e_steps = max(1, min(args.steps, 64))
     barrier()
@@ -362,7 +374,10 @@ def gpu_arm(args, rank, world, local_rank):
     e2.record()
     for s in range(e_steps):
         dev_in.copy_(host_in[s % NI], non_blocking=True)
-        step(dev_in)
+        dev_q.copy_(host_q[s % NI], non_blocking=True)
+        step(s, dev_in, dev_q)
+        for l in range(Ly):
+            outbuf[l].copy_(outs[l])
         host_out.copy_(outbuf, non_blocking=True)
     e3.record()
     torch.cuda.synchronize()
@@ -380,7 +395,7 @@ def gpu_arm(args, rank, world, local_rank):
     vc = cache.block_pool_v.view(cache.total_blocks, T, D)
     gl = cache.global_lengths
     seq_l = [(gl[l] + W).to(torch.int32).contiguous() for l in range(Ly)]
-    qd = inputs[0, :, :, :Hq].transpose(2, 3)  # (Ly, B, 1, Hq, D) view
+    qd = qbuf[0]  # (Ly, B, 1, Hq, D)
     od = torch.empty(B, 1, Hq, D, dtype=torch.bfloat16, device=dev)
     reps = 3
     for l in range(Ly):
@@ -404,8 +419,7 @@ def gpu_arm(args, rank, world, local_rank):
     prof = os.path.join(HERE, "profiles", "paged_decode_traffic.json")
     if os.path.exists(prof):
         try:
-            d = json.load(open(prof))
-            traffic = float(d["dram_bytes_per_token"]) * (int(sl.sum()) / Ly)
+            traffic = float(json.load(open(prof))["dram_bytes_per_algorithmic_byte"]) * kbytes
         except Exception:
             traffic = None
 
@@ -421,7 +435,7 @@ def gpu_arm(args, rank, world, local_rank):
                        "l2": "inputs larger than L2 (~62 GB cache), no flush", "parallelism": f"dp{world} (sequences)",
                        **CFG},
             "hbm_gbs_step": bytes_step / (ms_step / 1e3) / 1e9,
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(inputs[0].numel() * 2),
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int((inputs[0][..., Hq:].numel() + qbuf[0].numel()) * 2),
                     "d2h_bytes_per_step": int(outbuf.numel() * 2)},
             "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
@@ -435,13 +449,128 @@ def gpu_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# prefill workload: 400K tokens, 32 layers, ~30 % admitted
+# ----------------------------------------------------------------------------
+PCFG = dict(model="Llama-3.1-8B-shaped", layers=32, seq_len=400000, q_heads=32, kv_heads=8, head_dim=128,
+            window=4096, page=16, admit="~30% mean per head", max_tokens_per_head=401000,
+            gate="pre_k->64->1 GELU sigmoid", threshold=0.5)
+
+
+def useful_flops(cc, L, W, D, G, blk=64):
+    """4*D FLOPs per unmasked (q, k) pair of the vertical-slash mask, summed over query heads."""
+    B, Hk, R = cc.shape
+    q = np.arange(L)
+    s = (q // blk) * blk
+    band = q - np.maximum(0, s - W + 1) + 1  # causal band keys of each query
+    rows_per_block = np.bincount(q // blk, minlength=R)
+    pairs = cc.astype(np.int64) * rows_per_block[None, None, :]
+    return 4.0 * D * G * (float(pairs.sum()) + B * Hk * float(band.sum()))
+
+
+def prefill_arm(args, rank, world, local_rank):
+    import torch
+    import wgkv
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    Ly, L, Hq, Hk, D, W, T = (PCFG[k] for k in ("layers", "seq_len", "q_heads", "kv_heads", "head_dim", "window", "page"))
+    if args.small:
+        Ly, L = 2, 65536
+    G = Hq // Hk
+    rng = np.random.default_rng(3 + rank)
+    rates = np.clip(rng.beta(3, 7, (Ly, Hk)), 0.05, 0.9)  # mean 0.3
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    q = torch.randn(1, L, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    kvp = torch.randn(1, L, 3 * Hk, D, generator=g, device=dev).to(torch.bfloat16)
+    k, v, pk = (kvp[:, :, i * Hk:(i + 1) * Hk].transpose(1, 2) for i in range(3))
+    # gates calibrated per (layer, head) to the drawn rates
+    CFG_save = dict(CFG)
+    CFG["layers"] = Ly
+    layers = build_layers(dev, np.repeat(rates[:, None, :], 1, axis=1), seed=5 + rank)
+    CFG.update(CFG_save)
+    total = int(Ly * Hk * (W + 1.1 * rates.mean() * L + L * 0.05)) + Ly * Hk * 64
+    for a in layers:
+        a.config.max_total_tokens = total
+        a.config.max_tokens_per_head = PCFG["max_tokens_per_head"] if not args.small else L + 64
+
+    def run(n_layers):
+        cache = SimpleNamespace()
+        for l in range(n_layers):
+            a = layers[l]
+            a.g_predictors  # noqa
+            o, _, _ = a.self_attn_forward_patch(a, 3, None, cache, (1, L), q.transpose(1, 2), pk, k, v)
+        return cache
+
+    c = run(1)  # warm-up: one layer
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    del c
+    torch.cuda.empty_cache()
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    l0 = wgkv.lib.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    cache = run(Ly)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = wgkv.lib.launches - l0
+    ms = e0.elapsed_time(e1)
+    clocks = clk.stop() if clk else None
+    wgkv.check_errors()
+    admitted = int(cache.global_lengths.sum().item())
+    # useful FLOPs from each layer's indices, and the sparse attention kernel timed alone (layer 0's mask)
+    flops = 0.0
+    idx0 = None
+    for l in range(Ly):
+        gm = torch.empty(1, Hk, L, dtype=torch.uint8, device=dev)
+        layers[l].g_predictors.admit(pk, k, v, PCFG["threshold"], gm)
+        idx = wgkv.sparse_indices_into(gm, W, L, 64)
+        flops += useful_flops(idx[2].cpu().numpy(), L, W, D, G)
+        if l == 0:
+            idx0 = idx
+    torch.cuda.synchronize()
+    out = torch.empty_like(q)
+    wgkv.sparse_attn_func(q, kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk], *idx0, softmax_scale=D ** -0.5, out=out)
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    wgkv.sparse_attn_func(q, kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk], *idx0, softmax_scale=D ** -0.5, out=out)
+    e3.record()
+    torch.cuda.synchronize()
+    attn_ms = e2.elapsed_time(e3)
+    f0 = useful_flops(idx0[2].cpu().numpy(), L, W, D, G)
+    tf = f0 / (attn_ms / 1e3) / 1e12
+    try:
+        pk_tf = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"]), "measured"
+    except Exception:
+        pk_tf = 1590.0, "fallback"
+    line = {"metric": f"{L // 1000}K sparse-prefill ms ({Ly} layers)", "value": ms, "unit": "ms", "n_gpus": 1,
+            "steps": 1, "warmup": 1, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C3 prefill" + (" (small)" if args.small else ""), **PCFG, "layers": Ly,
+                       "seq_len": L},
+            "admitted_frac": admitted / (Ly * Hk * max(L - W, 1)),
+            "useful_tflops_total": flops / 1e12, "tflops_step": flops / (ms / 1e3) / 1e12,
+            "roofline": {"bound": "tensor", "kernel": "sparse_prefill_kernel", "achieved": tf, "peak": pk_tf[0],
+                         "peak_kind": pk_tf[1], "unit": "TFLOP/s", "frac": tf / pk_tf[0], "traffic": None,
+                         "ms_per_launch": attn_ms, "flops_per_launch": f0},
+            "gpu_launches": launches, "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
     args = ap.parse_args()
+    if args.small and args.workload == "decode":
+        CFG["layers"] = 2
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
@@ -454,7 +583,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        gpu_arm(args, rank, world, local_rank)
+        if args.workload == "prefill":
+            prefill_arm(args, rank, world, local_rank)
+        else:
+            gpu_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
