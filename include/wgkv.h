@@ -180,6 +180,9 @@ WGKV_API int wgkv_sparse_indices(const uint8_t* g_mask, int64_t m_sb, int64_t m_
  *   k,v (B, L, Hk, D) bf16, strides likewise; out (B, L, Hq, D) bf16 strided likewise
  *   block_count (R), block_offset (R, bo_stride), column_count (B, Hk, R), column_index (B, Hk, ci_stride)
  * Constraints: D in {64, 128}; block == 64; Hq % Hk == 0.
+ * Even GQA groups with 16-byte-aligned [B*L, H*D] row views run on the tcgen05 kernel (TMA + TMEM);
+ * other shapes on an mma.sync kernel.  `err` (device word, may be NULL) receives WGKV_ERR_TIMEOUT if
+ * a pipeline wait gives up.
  */
 WGKV_API int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const uint16_t* k,
                                  int64_t k_sb, int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb,
@@ -187,7 +190,7 @@ WGKV_API int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl, 
                                  int num_kv_heads, int head_dim, const int32_t* block_count,
                                  const int32_t* block_offset, int64_t bo_stride, const int32_t* column_count,
                                  const int32_t* column_index, int64_t ci_stride, float softmax_scale, uint16_t* out,
-                                 int64_t o_sb, int64_t o_sl, int64_t o_sh, void* stream);
+                                 int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, void* stream);
 
 /* ---- (a7, a8) ragged paged decode attention ----------------------------- */
 /*

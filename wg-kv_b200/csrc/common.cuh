@@ -13,11 +13,6 @@
 
 namespace wgkv {
 
-// Upper bound on polls of one mbarrier before a wait gives up and the kernel
-// reports WGKV_ERR_TIMEOUT (try_wait suspends for a while per poll, so this is
-// well above a second of waiting).
-constexpr long long kMaxPolls = 1ll << 26;
-
 WGKV_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -43,10 +38,20 @@ WGKV_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait on the phase with the given parity; false on timeout.
+WGKV_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on the phase with the given parity: gives up (returns false)
+// after about kWaitLimitNs of wall time, so a broken pipeline ends the kernel
+// with an error status instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 WGKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t addr = smem_u32(bar);
-  for (long long i = 0; i < kMaxPolls; ++i) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (long long i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n"
@@ -56,8 +61,12 @@ WGKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 255) == 0) {
+      const uint64_t now = global_ns();
+      if (i == 0) t0 = now;
+      else if (now - t0 > kWaitLimitNs) return false;
+    }
   }
-  return false;
 }
 
 // 2D tiled TMA load (no multicast) of box {x, y} into shared memory.

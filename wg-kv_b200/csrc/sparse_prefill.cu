@@ -15,6 +15,11 @@
 #include "runtime.h"
 
 namespace wgkv {
+int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const uint16_t* k, int64_t k_sb,
+                      int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int B,
+                      int L, int Hq, int Hk, int D, const int32_t* bc, const int32_t* bo, int64_t bo_stride,
+                      const int32_t* cc, const int32_t* ci, int64_t ci_stride, float scale, uint16_t* out,
+                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream);
 namespace {
 
 constexpr int kBlk = 64;  // query rows per block = keys per tile
@@ -240,7 +245,7 @@ extern "C" int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl
                                    int num_kv_heads, int head_dim, const int32_t* block_count,
                                    const int32_t* block_offset, int64_t bo_stride, const int32_t* column_count,
                                    const int32_t* column_index, int64_t ci_stride, float softmax_scale, uint16_t* out,
-                                   int64_t o_sb, int64_t o_sl, int64_t o_sh, void* stream) {
+                                   int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, void* stream) {
   if (!q || !k || !v || !out || !block_count || !block_offset || !column_count || !column_index) return WGKV_EINVAL;
   if (batch <= 0 || seq_len <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
   // 16-byte row gathers and 4-byte q/out accesses
@@ -248,6 +253,13 @@ extern "C" int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl
       ((k_sb | k_sl | k_sh | v_sb | v_sl | v_sh) % 8) || (reinterpret_cast<uintptr_t>(q) & 3) ||
       (reinterpret_cast<uintptr_t>(out) & 3) || ((q_sb | q_sl | q_sh | o_sb | o_sl | o_sh) & 1))
     return WGKV_EINVAL;
+  {
+    const int rc = sparse_prefill_tc(q, q_sb, q_sl, q_sh, k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, batch, seq_len,
+                                     num_q_heads, num_kv_heads, head_dim, block_count, block_offset, bo_stride,
+                                     column_count, column_index, ci_stride, softmax_scale, out, o_sb, o_sl, o_sh, err,
+                                     as_stream(stream));
+    if (rc != 1) return rc;  // handled by the tensor-core kernel
+  }
   PrefillParams p;
   p.q = q; p.k = k; p.v = v; p.out = out;
   p.q_sb = q_sb; p.q_sl = q_sl; p.q_sh = q_sh;

@@ -1,0 +1,397 @@
+// Block-sparse (vertical-slash) causal prefill attention on the 5th-gen
+// tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Same contract as the mma.sync kernel in sparse_prefill.cu (the attention
+// sparse_attn_func computes for generate_sparse_indices' indices, pinned by
+// utils/test_sparse_attn.py:34-93).  One CTA owns one 64-query row block of
+// one KV head and 2*NM query heads of its GQA group, i.e. NM M-tiles of 128
+// rows (two heads x 64 queries each) that share every K/V tile:
+//
+//   warp 0      TMA producer: Q once; per 64-key tile, K and V into 3-stage
+//               rings.  Admitted-column tiles are gathered with
+//               cp.async.bulk.tensor tile::gather4 (4 key rows per
+//               instruction, indices from column_index); band tiles are plain
+//               2D tiles.  SWIZZLE_128B, no multicast.
+//   warp 1      TMEM allocator + single-thread MMA issuer:
+//               S_t = Q_t K^T  (M=128, N=64, K=D; S double-buffered in TMEM)
+//               O_t += P_t V   (M=128, N=D, K=64; P from shared memory)
+//   warps 2..   one warpgroup per M-tile: reads S rows from TMEM (one row per
+//               thread), masks (column tail / causal band), online softmax in
+//               base 2 with a lazy running max (O is rescaled in TMEM only when
+//               the max grows by more than 2^8), writes P as bf16 into the
+//               canonical K-major SW128 layout, and finally normalises O.
+#include "common.cuh"
+#include "runtime.h"
+#include "tc.cuh"
+
+namespace wgkv {
+namespace {
+
+constexpr int kKeys = 64;  // keys per K/V tile
+constexpr int kKS = 3;     // K stages
+constexpr int kVS = 3;     // V stages
+constexpr float kRescaleThreshold = 8.f;  // log2 of the largest tolerated growth of unnormalised terms
+
+template <int D, int NM>
+struct Tc {
+  static constexpr int kDB = D / 64;               // 64-column boxes per row
+  static constexpr int kQTile = kDB * 16384;       // one M-tile of Q: kDB boxes x 128 rows x 128 B
+  static constexpr int kKV = kDB * kKeys * 128;    // one K or V stage
+  static constexpr int kP = 128 * 128;             // 128 rows x 64 keys x 2 B
+  static constexpr int kOffK = NM * kQTile;
+  static constexpr int kOffV = kOffK + kKS * kKV;
+  static constexpr int kOffP = kOffV + kVS * kKV;
+  static constexpr int kOffBar = kOffP + NM * kP;
+  static constexpr int kSmem = kOffBar + 512 + 1024;  // barriers + alignment slack
+  static constexpr int kThreads = 64 + 128 * NM;
+  static constexpr int kTmemCols = NM == 2 ? 512 : 256;
+};
+
+struct TcParams {
+  int B, L, Hk, G, R, n_hg;
+  const int32_t *bc, *bo, *cc, *ci;
+  int64_t bo_stride, ci_stride;
+  float scale_log2;
+  uint16_t* out;
+  int64_t o_sb, o_sl, o_sh;
+  int* err;
+};
+
+struct Bars {
+  uint64_t qfull;
+  uint64_t kfull[kKS], kempty[kKS];
+  uint64_t vfull[kVS], vempty[kVS];
+  uint64_t sfull[2][2], sfree[2][2];
+  uint64_t pfull[2], odone[2];
+  uint32_t tmem;
+};
+
+template <int D, int NM>
+__global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
+    sparse_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKg,
+                             const __grid_constant__ CUtensorMap tmVg, TcParams p) {
+  using C = Tc<D, NM>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bar = reinterpret_cast<Bars*>(sm + C::kOffBar);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const int i = p.R - 1 - blockIdx.x;  // heaviest row blocks first
+  const int hg = blockIdx.y % p.n_hg;
+  const int h = blockIdx.y / p.n_hg;
+  const int b = blockIdx.z;
+  const int s0 = i * 64;
+  const int hq0 = h * p.G + hg * 2 * NM;  // first query head of this CTA
+  const int ncol = p.cc[(int64_t(b) * p.Hk + h) * p.R + i];
+  const int nband = p.bc[i];
+  const int ntc = (ncol + kKeys - 1) / kKeys;
+  const int n = ntc + nband;
+  const int32_t* bo_row = p.bo + int64_t(i) * p.bo_stride;
+
+  if (tid == 0) {
+    mbar_init(&bar->qfull, 1);
+    for (int s = 0; s < kKS; ++s) { mbar_init(&bar->kfull[s], 1); mbar_init(&bar->kempty[s], 1); }
+    for (int s = 0; s < kVS; ++s) { mbar_init(&bar->vfull[s], 1); mbar_init(&bar->vempty[s], 1); }
+    for (int t = 0; t < 2; ++t) {
+      for (int u = 0; u < 2; ++u) { mbar_init(&bar->sfull[t][u], 1); mbar_init(&bar->sfree[t][u], 4); }
+      mbar_init(&bar->pfull[t], 4);
+      mbar_init(&bar->odone[t], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<C::kTmemCols>(&bar->tmem);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ================================ producer ================================
+    if (lane == 0) {
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmK);
+      prefetch_tensormap(&tmV);
+      prefetch_tensormap(&tmKg);
+      prefetch_tensormap(&tmVg);
+      mbar_arrive_expect_tx(&bar->qfull, NM * 2 * C::kDB * 8192);
+      for (int t = 0; t < NM; ++t)
+        for (int hh = 0; hh < 2; ++hh)
+          for (int d = 0; d < C::kDB; ++d)
+            tma_load_2d(sm + t * C::kQTile + d * 16384 + hh * 8192, &tmQ, &bar->qfull,
+                        (hq0 + 2 * t + hh) * D + d * 64, b * p.L + s0);
+    }
+    const int32_t* cib = p.ci + (int64_t(b) * p.Hk + h) * p.ci_stride;
+    // lane -> (4-row group, 64-column box) of a gathered tile
+    const int grp = C::kDB == 2 ? (lane & 15) : lane;
+    const int dl = C::kDB == 2 ? (lane >> 4) : 0;
+    for (int j = 0; j < n && ok; ++j) {
+      const bool col = j < ntc;
+      int rows4[4] = {0, 0, 0, 0};
+      if (col && grp < 16) {
+        for (int r = 0; r < 4; ++r) {
+          int e = j * kKeys + grp * 4 + r;
+          e = e < ncol ? e : ncol - 1;  // past the tail: any valid row (masked in the softmax)
+          rows4[r] = b * p.L + __ldg(cib + e);
+        }
+      }
+      const int off = col ? 0 : __ldg(bo_row + (j - ntc));
+      for (int kv = 0; kv < 2; ++kv) {
+        const int nst = kv ? kVS : kKS;
+        const int s = j % nst;
+        const uint32_t ph = (j / nst) & 1;
+        uint64_t* full = kv ? &bar->vfull[s] : &bar->kfull[s];
+        uint64_t* empty = kv ? &bar->vempty[s] : &bar->kempty[s];
+        if (!mbar_wait(empty, ph ^ 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+        uint8_t* st = sm + (kv ? C::kOffV : C::kOffK) + s * C::kKV;
+        if (lane == 0) mbar_arrive_expect_tx(full, C::kKV);
+        __syncwarp();
+        if (col) {
+          if (grp < 16)
+            tma_gather4(st + dl * 8192 + grp * 512, kv ? &tmVg : &tmKg, full, h * D + dl * 64, rows4[0], rows4[1],
+                        rows4[2], rows4[3]);
+        } else if (lane == 0) {
+          for (int d = 0; d < C::kDB; ++d)
+            tma_load_2d(st + d * 8192, kv ? &tmV : &tmK, full, h * D + d * 64, b * p.L + off);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ============================ MMA issuer (1 thread) ============================
+    if (lane == 0) {
+      const uint32_t id_qk = umma_idesc_bf16(128, kKeys, 0, 0);
+      const uint32_t id_pv = umma_idesc_bf16(128, D, 0, 1);
+      if (!mbar_wait(&bar->qfull, 0)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
+      for (int j = 0; j <= n && ok; ++j) {
+        if (j < n) {
+          const int ks = j % kKS;
+          if (!mbar_wait(&bar->kfull[ks], (j / kKS) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+          const uint32_t kst = smem_u32(sm + C::kOffK + ks * C::kKV);
+          const int sb = j & 1;
+          for (int t = 0; t < NM; ++t) {
+            if (!mbar_wait(&bar->sfree[t][sb], ((j >> 1) & 1) ^ 1)) {
+              set_error(p.err, WGKV_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t qt = smem_u32(sm + t * C::kQTile);
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint64_t a = umma_desc_sw128(qt + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
+              const uint64_t bb = umma_desc_sw128(kst + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024);
+              umma_ss(tmem + t * 256 + sb * 64, a, bb, id_qk, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&bar->sfull[t][sb]);
+          }
+          if (!ok) break;
+          umma_commit(&bar->kempty[ks]);
+        }
+        if (j > 0) {
+          const int jj = j - 1;
+          const int vs = jj % kVS;
+          if (!mbar_wait(&bar->vfull[vs], (jj / kVS) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+          const uint32_t vst = smem_u32(sm + C::kOffV + vs * C::kKV);
+          for (int t = 0; t < NM; ++t) {
+            if (!mbar_wait(&bar->pfull[t], jj & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+            tc_fence_after();
+            const uint32_t pt = smem_u32(sm + C::kOffP + t * C::kP);
+#pragma unroll
+            for (int k = 0; k < kKeys / 16; ++k) {
+              const uint64_t a = umma_desc_sw128(pt + k * 32, 16, 1024);
+              const uint64_t bb = umma_desc_sw128(vst + k * 2048, 8192, 1024);
+              umma_ss(tmem + t * 256 + 128, a, bb, id_pv, (jj > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar->odone[t]);
+          }
+          if (!ok) break;
+          umma_commit(&bar->vempty[vs]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ============================ softmax warpgroups ============================
+    const int t = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;         // TMEM lane = row of M-tile t
+    const int hh = 2 * t + (row >> 6);
+    const int q = s0 + (row & 63);
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
+    uint8_t* prow = sm + C::kOffP + t * C::kP + row * 128;
+    const float sc = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    for (int j = 0; j < n && ok; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&bar->sfull[t][sb], (j >> 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+      tc_fence_after();
+      float sv[64];
+      tmem_ld32(trow + sb * 64, sv);
+      tmem_ld32(trow + sb * 64 + 32, sv + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->sfree[t][sb]);
+      // mask + tile max
+      float mt = -INFINITY;
+      if (j < ntc) {
+        const int nv = ncol - j * kKeys;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          sv[c] = c < nv ? sv[c] * sc : -INFINITY;
+          mt = fmaxf(mt, sv[c]);
+        }
+      } else {
+        const int off = __ldg(bo_row + (j - ntc));
+        const int lim = min(q, p.L - 1) - off;  // keys off + c with c <= lim are visible
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          sv[c] = c <= lim ? sv[c] * sc : -INFINITY;
+          mt = fmaxf(mt, sv[c]);
+        }
+      }
+      float alpha = 1.f;
+      bool need = false;
+      if (mt > m_used + kRescaleThreshold) {  // also true on the first visible key (m_used = -inf)
+        need = true;
+        alpha = exp2f(m_used - mt);  // 0 when m_used = -inf
+        m_used = mt;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        const float p0 = exp2f(sv[c] - base), p1 = exp2f(sv[c + 1] - base);
+        sum += p0 + p1;
+        pk[c >> 1] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + sum;
+      if (j > 0) {
+        // PV(j-1) must be done before P is overwritten and before O is rescaled
+        if (!mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffff, need && alpha != 1.f)) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            float ov[32];
+            tmem_ld32(trow + 128 + c0, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) ov[c] *= alpha;
+            tmem_st32(trow + 128 + c0, ov);
+          }
+          tmem_wait_st();
+        }
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const uint4 v = make_uint4(pk[c8 * 4], pk[c8 * 4 + 1], pk[c8 * 4 + 2], pk[c8 * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->pfull[t]);
+    }
+    // ---- epilogue: O / l -> bf16 ----
+    if (ok && n > 0) {
+      if (!mbar_wait(&bar->odone[t], (n - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
+    }
+    tc_fence_after();
+    const bool any = l > 0.f;  // a row that saw no key (degenerate index sets only) writes zeros
+    const float inv = any ? 1.f / l : 0.f;
+    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      float ov[32];
+      tmem_ld32(trow + 128 + c0, ov);
+      tmem_wait_ld();
+      if (ok && q < p.L) {
+        if (!any) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) ov[c] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 v;
+          v.x = pack_bf16x2(ov[c] * inv, ov[c + 1] * inv);
+          v.y = pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv);
+          v.z = pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv);
+          v.w = pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + c0 + c) = v;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<C::kTmemCols>(tmem);
+  }
+}
+
+template <int D, int NM>
+int launch_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q_sl, int64_t k_sl, int64_t v_sl,
+              int Hq, int Hk, const TcParams& p, cudaStream_t stream) {
+  using C = Tc<D, NM>;
+  CUtensorMap mq, mk, mv, mkg, mvg;
+  const uint64_t rows = uint64_t(p.B) * p.L;
+  if (!encode_2d_bf16(&mq, q, uint64_t(Hq) * D, rows, q_sl, 64, 64, true)) return WGKV_ECUDA;
+  if (!encode_2d_bf16(&mk, k, uint64_t(Hk) * D, rows, k_sl, 64, 64, true)) return WGKV_ECUDA;
+  if (!encode_2d_bf16(&mv, v, uint64_t(Hk) * D, rows, v_sl, 64, 64, true)) return WGKV_ECUDA;
+  if (!encode_2d_bf16(&mkg, k, uint64_t(Hk) * D, rows, k_sl, 64, 1, true)) return WGKV_ECUDA;
+  if (!encode_2d_bf16(&mvg, v, uint64_t(Hk) * D, rows, v_sl, 64, 1, true)) return WGKV_ECUDA;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(sparse_prefill_tc_kernel<D, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmem) != cudaSuccess)
+      return WGKV_ECUDA;
+    attr[dev] = true;
+  }
+  dim3 grid(p.R, p.Hk * p.n_hg, p.B);
+  sparse_prefill_tc_kernel<D, NM><<<grid, C::kThreads, C::kSmem, stream>>>(mq, mk, mv, mkg, mvg, p);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+}  // namespace
+
+// Used by wgkv_sparse_prefill when the problem fits the tensor-core kernel
+// (even GQA group, D in {64, 128}, each tensor a 2D [B*L, H*D] view with 16-byte rows).
+// Returns 1 when it does not apply (the caller falls back), else a WGKV status.
+int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh, const uint16_t* k, int64_t k_sb,
+                      int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int B,
+                      int L, int Hq, int Hk, int D, const int32_t* bc, const int32_t* bo, int64_t bo_stride,
+                      const int32_t* cc, const int32_t* ci, int64_t ci_stride, float scale, uint16_t* out,
+                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream) {
+  const int G = Hq / Hk;
+  if (G % 2 != 0 || (D != 64 && D != 128)) return 1;
+  if (q_sh != D || k_sh != D || v_sh != D) return 1;
+  if ((B > 1) && (q_sb != int64_t(L) * q_sl || k_sb != int64_t(L) * k_sl || v_sb != int64_t(L) * v_sl)) return 1;
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+        reinterpret_cast<uintptr_t>(out)) & 15) ||
+      ((q_sl | k_sl | v_sl) % 8) || ((o_sb | o_sl | o_sh) % 8))
+    return 1;
+  if (int64_t(B) * L >= (int64_t(1) << 31)) return 1;
+  TcParams p;
+  p.B = B; p.L = L; p.Hk = Hk; p.G = G; p.R = (L + 63) / 64;
+  p.bc = bc; p.bo = bo; p.cc = cc; p.ci = ci; p.bo_stride = bo_stride; p.ci_stride = ci_stride;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = out; p.o_sb = o_sb; p.o_sl = o_sl; p.o_sh = o_sh;
+  p.err = err;
+  if (G % 4 == 0) {
+    p.n_hg = G / 4;
+    return D == 128 ? launch_tc<128, 2>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream)
+                    : launch_tc<64, 2>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream);
+  }
+  p.n_hg = G / 2;
+  return D == 128 ? launch_tc<128, 1>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream)
+                  : launch_tc<64, 1>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream);
+}
+
+}  // namespace wgkv

@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from ._lib import check, lib
-from .runtime import require_cuda, stream_ptr
+from .runtime import err_word, require_cuda, stream_ptr
 
 
 def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_index, softmax_scale=None,
@@ -53,7 +53,7 @@ def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_in
                                  k.stride(1), k.stride(2), v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), B, L,
                                  Hq, Hk, D, bc.data_ptr(), bo.data_ptr(), bo.stride(0), cc.data_ptr(), ci.data_ptr(),
                                  ci.stride(1), float(softmax_scale), out.data_ptr(), out.stride(0), out.stride(1),
-                                 out.stride(2), stream_ptr(q.device))
+                                 out.stride(2), err_word(q.device).data_ptr(), stream_ptr(q.device))
     check(st, "wgkv_sparse_prefill")
     return out
 
