@@ -192,6 +192,27 @@ WGKV_API int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl, 
                                  const int32_t* column_index, int64_t ci_stride, float softmax_scale, uint16_t* out,
                                  int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, void* stream);
 
+/*
+ * Same attention, reading the admitted-column keys from the paged pool instead of gathering them
+ * from k / v: after wgkv_prefill_admit, the admitted tokens of (b, h) among the first L - window
+ * sit in token order in contiguous pool rows starting at table[(b*Hk + h)*table_stride +
+ * table_first] * page_size (table = the layer's block_table, table_first = window / page_size),
+ * which is exactly column_index's order; every column the indices use lies in that range.  The
+ * column tiles then load as plain 2D TMA tiles.  k / v still supply the local band.  The indices
+ * must come from the mask the pool was filled with.  Internal to prefill_wrapper's fast path (the
+ * reference has no separate interface for it; it computes sparse_attn_func's result).
+ */
+WGKV_API int wgkv_sparse_prefill_pooled(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                                        const uint16_t* k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                                        const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int batch,
+                                        int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                        const int32_t* block_count, const int32_t* block_offset, int64_t bo_stride,
+                                        const int32_t* column_count, const int32_t* column_index, int64_t ci_stride,
+                                        float softmax_scale, uint16_t* out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
+                                        const uint16_t* pool_k, const uint16_t* pool_v, int64_t pool_rows,
+                                        const int32_t* table, int64_t table_stride, int table_first, int page_size,
+                                        int* err, void* stream);
+
 /* ---- (a7, a8) ragged paged decode attention ----------------------------- */
 /*
  * out[b, 0, hq, :] = softmax(q[b, 0, hq, :] . K_h^T * scale) V_h, h = hq / G,

@@ -210,3 +210,31 @@ def test_head_capacity_reports(wgkv):
     torch.cuda.synchronize()
     with pytest.raises(AssertionError, match="max_tokens_per_head"):
         wgkv.check_errors()
+
+
+@pytest.mark.parametrize("B,Hk,G,D", [(2, 4, 4, 128), (1, 2, 2, 64), (2, 2, 3, 128)])
+def test_pooled_prefill_matches_gather(wgkv, B, Hk, G, D):
+    """Reading admitted columns from the compacted pool gives the gathered result (same bits)."""
+    from types import SimpleNamespace
+    rng = np.random.default_rng(B * 100 + Hk * 10 + G + D)
+    L, W, T = 3000, 256, 16
+    Hq = Hk * G
+    q = O.randn_bf16(rng, (B, L, Hq, D))
+    k = O.randn_bf16(rng, (B, L, Hk, D))
+    v = O.randn_bf16(rng, (B, L, Hk, D))
+    g = rng.random((B, Hk, L)) < 0.3
+    cache = SimpleNamespace()
+    a = SimpleNamespace(layer_idx=0, head_dim=D, scaling=D ** -0.5,
+                        config=SimpleNamespace(num_hidden_layers=1, num_key_value_heads=Hk, local_window_size=W,
+                                               block_size=T, max_total_tokens=B * Hk * (L + W) + 64 * T,
+                                               max_tokens_per_head=L + W))
+    wgkv.attach(a, a.config)
+    tq, tk, tv = to_bf16(q), to_bf16(k), to_bf16(v)
+    gm = torch.from_numpy(g.astype(np.uint8)).cuda()
+    pooled = wgkv.prefill_wrapper(a, cache, tq.transpose(1, 2), None, tk.transpose(1, 2), tv.transpose(1, 2), B, L,
+                                  tq.device, gm, W // T)
+    idx = wgkv.generate_sparse_indices(gm, W, B, Hk, L, gm.device)
+    gathered = wgkv.sparse_attn_func(tq, tk, tv, *idx, softmax_scale=D ** -0.5)
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    assert torch.equal(pooled, gathered)

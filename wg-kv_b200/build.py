@@ -16,8 +16,9 @@ import sys
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
-OUT = os.path.join(PKG, "wgkv", "libwgkv.so")
-BUILD = os.path.join(PKG, "_build")
+# WGKV_LIB_OUT / WGKV_BUILD_DIR / WGKV_EXTRA_NVCC redirect a build (e.g. a variant with extra -D flags)
+OUT = os.environ.get("WGKV_LIB_OUT", os.path.join(PKG, "wgkv", "libwgkv.so"))
+BUILD = os.environ.get("WGKV_BUILD_DIR", os.path.join(PKG, "_build"))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -32,6 +33,7 @@ def flags(debug=False):
          "--expt-relaxed-constexpr", "-Xptxas", "-v" if os.environ.get("WGKV_PTXAS_V") else "-O3"]
     if debug:
         f += ["-DWGKV_DEBUG=1"]
+    f += os.environ.get("WGKV_EXTRA_NVCC", "").split()
     return ARCH + f
 
 

@@ -19,7 +19,9 @@ int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_s
                       int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int B,
                       int L, int Hq, int Hk, int D, const int32_t* bc, const int32_t* bo, int64_t bo_stride,
                       const int32_t* cc, const int32_t* ci, int64_t ci_stride, float scale, uint16_t* out,
-                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream);
+                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream,
+                      const uint16_t* pool_k, const uint16_t* pool_v, int64_t pool_rows, const int32_t* table,
+                      int64_t t_stride, int t_first, int t_page);
 namespace {
 
 constexpr int kBlk = 64;  // query rows per block = keys per tile
@@ -257,7 +259,7 @@ extern "C" int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl
     const int rc = sparse_prefill_tc(q, q_sb, q_sl, q_sh, k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, batch, seq_len,
                                      num_q_heads, num_kv_heads, head_dim, block_count, block_offset, bo_stride,
                                      column_count, column_index, ci_stride, softmax_scale, out, o_sb, o_sl, o_sh, err,
-                                     as_stream(stream));
+                                     as_stream(stream), nullptr, nullptr, 0, nullptr, 0, 0, 0);
     if (rc != 1) return rc;  // handled by the tensor-core kernel
   }
   PrefillParams p;
@@ -278,4 +280,30 @@ extern "C" int wgkv_sparse_prefill(const uint16_t* q, int64_t q_sb, int64_t q_sl
   if (head_dim == 128) return hpc == 2 ? launch<128, 2>(p, s) : launch<128, 1>(p, s);
   if (head_dim == 64) return hpc == 2 ? launch<64, 2>(p, s) : launch<64, 1>(p, s);
   return WGKV_EINVAL;
+}
+
+extern "C" int wgkv_sparse_prefill_pooled(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_sh,
+                                          const uint16_t* k, int64_t k_sb, int64_t k_sl, int64_t k_sh,
+                                          const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int batch,
+                                          int seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                          const int32_t* block_count, const int32_t* block_offset, int64_t bo_stride,
+                                          const int32_t* column_count, const int32_t* column_index,
+                                          int64_t ci_stride, float softmax_scale, uint16_t* out, int64_t o_sb,
+                                          int64_t o_sl, int64_t o_sh, const uint16_t* pool_k, const uint16_t* pool_v,
+                                          int64_t pool_rows, const int32_t* table, int64_t table_stride,
+                                          int table_first, int page_size, int* err, void* stream) {
+  if (!q || !k || !v || !out || !block_count || !block_offset || !column_count || !column_index) return WGKV_EINVAL;
+  if (batch <= 0 || seq_len <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
+  if (!pool_k || !pool_v || !table || pool_rows <= 0 || pool_rows >= (int64_t(1) << 31) || page_size <= 0)
+    return WGKV_EINVAL;
+  const int rc = sparse_prefill_tc(q, q_sb, q_sl, q_sh, k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, batch, seq_len,
+                                   num_q_heads, num_kv_heads, head_dim, block_count, block_offset, bo_stride,
+                                   column_count, column_index, ci_stride, softmax_scale, out, o_sb, o_sl, o_sh, err,
+                                   as_stream(stream), pool_k, pool_v, pool_rows, table, table_stride, table_first,
+                                   page_size);
+  if (rc != 1) return rc;
+  // shapes the tensor-core kernel does not take: the gathering path reads the same columns from k / v
+  return wgkv_sparse_prefill(q, q_sb, q_sl, q_sh, k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, batch, seq_len,
+                             num_q_heads, num_kv_heads, head_dim, block_count, block_offset, bo_stride, column_count,
+                             column_index, ci_stride, softmax_scale, out, o_sb, o_sl, o_sh, err, stream);
 }

@@ -47,6 +47,14 @@ struct Tc {
   static constexpr int kTmemCols = NM == 2 ? 512 : 256;
 };
 
+// 2^x on the SFU (ex2.approx, flush-to-zero): the softmax terms are rounded to
+// bf16 before PV, so its ~2-ulp fp32 error is far below what the result keeps.
+WGKV_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct TcParams {
   int B, L, Hk, G, R, n_hg;
   const int32_t *bc, *bo, *cc, *ci;
@@ -55,6 +63,10 @@ struct TcParams {
   uint16_t* out;
   int64_t o_sb, o_sl, o_sh;
   int* err;
+  // pooled mode: admitted columns of (b, h) are pool rows table[(b*Hk+h)*t_stride + t_first] * t_page + c
+  const int32_t* table;
+  int64_t t_stride;
+  int t_first, t_page;
 };
 
 struct Bars {
@@ -66,11 +78,12 @@ struct Bars {
   uint32_t tmem;
 };
 
-template <int D, int NM>
+template <int D, int NM, bool POOL>
 __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
     sparse_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKg,
-                             const __grid_constant__ CUtensorMap tmVg, TcParams p) {
+                             const __grid_constant__ CUtensorMap tmVg, const __grid_constant__ CUtensorMap tmKp,
+                             const __grid_constant__ CUtensorMap tmVp, TcParams p) {
   using C = Tc<D, NM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -115,6 +128,10 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
       prefetch_tensormap(&tmV);
       prefetch_tensormap(&tmKg);
       prefetch_tensormap(&tmVg);
+      if (POOL) {
+        prefetch_tensormap(&tmKp);
+        prefetch_tensormap(&tmVp);
+      }
       mbar_arrive_expect_tx(&bar->qfull, NM * 2 * C::kDB * 8192);
       for (int t = 0; t < NM; ++t)
         for (int hh = 0; hh < 2; ++hh)
@@ -126,17 +143,34 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
     // lane -> (4-row group, 64-column box) of a gathered tile
     const int grp = C::kDB == 2 ? (lane & 15) : lane;
     const int dl = C::kDB == 2 ? (lane >> 4) : 0;
-    for (int j = 0; j < n && ok; ++j) {
-      const bool col = j < ntc;
-      int rows4[4] = {0, 0, 0, 0};
-      if (col && grp < 16) {
+    // gather indices are fetched two tiles ahead so their latency hides behind the stage waits
+    const int pool_row0 =
+        POOL && ncol > 0 ? __ldg(p.table + (int64_t(b) * p.Hk + h) * p.t_stride + p.t_first) * p.t_page : 0;
+    auto fetch = [&](int j, int* r4) {
+      // pooled mode gathers only the partial last column tile (full tiles are contiguous pool rows;
+      // rows past a head's admitted count may hold anything, so they are not read)
+      if (j < ntc && (!POOL || ncol - j * kKeys < kKeys) && grp < 16) {
+#pragma unroll
         for (int r = 0; r < 4; ++r) {
           int e = j * kKeys + grp * 4 + r;
           e = e < ncol ? e : ncol - 1;  // past the tail: any valid row (masked in the softmax)
-          rows4[r] = b * p.L + __ldg(cib + e);
+          r4[r] = __ldg(cib + e);
         }
       }
-      const int off = col ? 0 : __ldg(bo_row + (j - ntc));
+    };
+    int pre0[4] = {0, 0, 0, 0}, pre1[4] = {0, 0, 0, 0};
+    fetch(0, pre0);
+    fetch(1, pre1);
+    for (int j = 0; j < n && ok; ++j) {
+      const bool col = j < ntc;
+      int rows4[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        rows4[r] = b * p.L + pre0[r];
+        pre0[r] = pre1[r];
+      }
+      fetch(j + 2, pre1);
+      const int off = col ? (POOL ? pool_row0 + j * kKeys : 0) : __ldg(bo_row + (j - ntc));
       for (int kv = 0; kv < 2; ++kv) {
         const int nst = kv ? kVS : kKS;
         const int s = j % nst;
@@ -147,7 +181,11 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
         uint8_t* st = sm + (kv ? C::kOffV : C::kOffK) + s * C::kKV;
         if (lane == 0) mbar_arrive_expect_tx(full, C::kKV);
         __syncwarp();
-        if (col) {
+        if (POOL && col && ncol - j * kKeys >= kKeys) {
+          // a full tile of compacted admitted columns: 64 contiguous pool rows
+          if (lane == 0)
+            for (int d = 0; d < C::kDB; ++d) tma_load_2d(st + d * 8192, kv ? &tmVp : &tmKp, full, d * 64, off);
+        } else if (col) {
           if (grp < 16)
             tma_gather4(st + dl * 8192 + grp * 512, kv ? &tmVg : &tmKg, full, h * D + dl * 64, rows4[0], rows4[1],
                         rows4[2], rows4[3]);
@@ -234,24 +272,21 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->sfree[t][sb]);
-      // mask + tile max
-      float mt = -INFINITY;
-      if (j < ntc) {
-        const int nv = ncol - j * kKeys;
+      // mask (raw scores; the positive scale is applied inside the exponent) + tile max
+      float mraw = -INFINITY;
+      if (j < ntc && ncol - j * kKeys >= kKeys) {  // full admitted-column tile: nothing to mask
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          sv[c] = c < nv ? sv[c] * sc : -INFINITY;
-          mt = fmaxf(mt, sv[c]);
-        }
+        for (int c = 0; c < 64; c += 2) mraw = fmaxf(mraw, fmaxf(sv[c], sv[c + 1]));
       } else {
-        const int off = __ldg(bo_row + (j - ntc));
-        const int lim = min(q, p.L - 1) - off;  // keys off + c with c <= lim are visible
+        const int lim = j < ntc ? ncol - j * kKeys - 1                              // column tail
+                                : min(q, p.L - 1) - __ldg(bo_row + (j - ntc));      // causal band
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          sv[c] = c <= lim ? sv[c] * sc : -INFINITY;
-          mt = fmaxf(mt, sv[c]);
+          sv[c] = c <= lim ? sv[c] : -INFINITY;
+          mraw = fmaxf(mraw, sv[c]);
         }
       }
+      const float mt = mraw * sc;
       float alpha = 1.f;
       bool need = false;
       if (mt > m_used + kRescaleThreshold) {  // also true on the first visible key (m_used = -inf)
@@ -259,15 +294,17 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
         alpha = exp2f(m_used - mt);  // 0 when m_used = -inf
         m_used = mt;
       }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
+      const float nbase = m_used == -INFINITY ? 0.f : -m_used;
+      float sum0 = 0.f, sum1 = 0.f;
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        const float p0 = exp2f(sv[c] - base), p1 = exp2f(sv[c + 1] - base);
-        sum += p0 + p1;
+        const float p0 = fast_exp2(fmaf(sv[c], sc, nbase)), p1 = fast_exp2(fmaf(sv[c + 1], sc, nbase));
+        sum0 += p0;
+        sum1 += p1;
         pk[c >> 1] = pack_bf16x2(p0, p1);
       }
+      const float sum = sum0 + sum1;
       l = l * alpha + sum;
       if (j > 0) {
         // PV(j-1) must be done before P is overwritten and before O is rescaled
@@ -334,9 +371,10 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
   }
 }
 
-template <int D, int NM>
+template <int D, int NM, bool POOL>
 int launch_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q_sl, int64_t k_sl, int64_t v_sl,
-              int Hq, int Hk, const TcParams& p, cudaStream_t stream) {
+              int Hq, int Hk, const uint16_t* pool_k, const uint16_t* pool_v, int64_t pool_rows, const TcParams& p,
+              cudaStream_t stream) {
   using C = Tc<D, NM>;
   CUtensorMap mq, mk, mv, mkg, mvg;
   const uint64_t rows = uint64_t(p.B) * p.L;
@@ -345,17 +383,22 @@ int launch_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q
   if (!encode_2d_bf16(&mv, v, uint64_t(Hk) * D, rows, v_sl, 64, 64, true)) return WGKV_ECUDA;
   if (!encode_2d_bf16(&mkg, k, uint64_t(Hk) * D, rows, k_sl, 64, 1, true)) return WGKV_ECUDA;
   if (!encode_2d_bf16(&mvg, v, uint64_t(Hk) * D, rows, v_sl, 64, 1, true)) return WGKV_ECUDA;
+  CUtensorMap mkp = mkg, mvp = mvg;  // pool maps (only read in pooled mode)
+  if (POOL) {
+    if (!encode_2d_bf16(&mkp, pool_k, D, uint64_t(pool_rows), D, 64, 64, true)) return WGKV_ECUDA;
+    if (!encode_2d_bf16(&mvp, pool_v, D, uint64_t(pool_rows), D, 64, 64, true)) return WGKV_ECUDA;
+  }
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(sparse_prefill_tc_kernel<D, NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(sparse_prefill_tc_kernel<D, NM, POOL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmem) != cudaSuccess)
       return WGKV_ECUDA;
     attr[dev] = true;
   }
   dim3 grid(p.R, p.Hk * p.n_hg, p.B);
-  sparse_prefill_tc_kernel<D, NM><<<grid, C::kThreads, C::kSmem, stream>>>(mq, mk, mv, mkg, mvg, p);
+  sparse_prefill_tc_kernel<D, NM, POOL><<<grid, C::kThreads, C::kSmem, stream>>>(mq, mk, mv, mkg, mvg, mkp, mvp, p);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -368,7 +411,9 @@ int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_s
                       int64_t k_sl, int64_t k_sh, const uint16_t* v, int64_t v_sb, int64_t v_sl, int64_t v_sh, int B,
                       int L, int Hq, int Hk, int D, const int32_t* bc, const int32_t* bo, int64_t bo_stride,
                       const int32_t* cc, const int32_t* ci, int64_t ci_stride, float scale, uint16_t* out,
-                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream) {
+                      int64_t o_sb, int64_t o_sl, int64_t o_sh, int* err, cudaStream_t stream,
+                      const uint16_t* pool_k, const uint16_t* pool_v, int64_t pool_rows, const int32_t* table,
+                      int64_t t_stride, int t_first, int t_page) {
   const int G = Hq / Hk;
   if (G % 2 != 0 || (D != 64 && D != 128)) return 1;
   if (q_sh != D || k_sh != D || v_sh != D) return 1;
@@ -384,14 +429,20 @@ int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_s
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out; p.o_sb = o_sb; p.o_sl = o_sl; p.o_sh = o_sh;
   p.err = err;
+  p.table = table; p.t_stride = t_stride; p.t_first = t_first; p.t_page = t_page;
+  const bool pool = pool_k != nullptr;
+  if (pool && (!pool_v || !table || ((reinterpret_cast<uintptr_t>(pool_k) | reinterpret_cast<uintptr_t>(pool_v)) & 15)))
+    return WGKV_EINVAL;
+#define WGKV_TC_LAUNCH(DD, NMM)                                                                            \
+  (pool ? launch_tc<DD, NMM, true>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream) \
+        : launch_tc<DD, NMM, false>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream))
   if (G % 4 == 0) {
     p.n_hg = G / 4;
-    return D == 128 ? launch_tc<128, 2>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream)
-                    : launch_tc<64, 2>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream);
+    return D == 128 ? WGKV_TC_LAUNCH(128, 2) : WGKV_TC_LAUNCH(64, 2);
   }
   p.n_hg = G / 2;
-  return D == 128 ? launch_tc<128, 1>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream)
-                  : launch_tc<64, 1>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, p, stream);
+  return D == 128 ? WGKV_TC_LAUNCH(128, 1) : WGKV_TC_LAUNCH(64, 1);
+#undef WGKV_TC_LAUNCH
 }
 
 }  // namespace wgkv

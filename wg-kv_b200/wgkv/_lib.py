@@ -13,7 +13,7 @@ import os
 import re
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "libwgkv.so")
+LIB_PATH = os.environ.get("WGKV_LIB", os.path.join(_PKG, "libwgkv.so"))
 HEADER = os.path.join(os.path.dirname(os.path.dirname(_PKG)), "include", "wgkv.h")
 
 _CTYPES = {
@@ -89,7 +89,8 @@ class _Lib:
 
 # kernels each compute entry point launches (for the benchmark's launch count)
 KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_append": 1, "wgkv_promote": 1,
-                    "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1}
+                    "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1, "wgkv_sparse_prefill_pooled": 1,
+                    "wgkv_paged_decode_noalloc": 1}
 
 
 lib = _Lib()

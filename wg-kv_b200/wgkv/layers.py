@@ -25,6 +25,7 @@ import torch
 from ._lib import check, lib
 from .indices import sparse_indices_into
 from .pool import init_pool, pool_ref
+from .prefill import sparse_attn_func, sparse_attn_func_pooled, sparse_attn_func_wrapper
 from .runtime import stream_ptr, workspace
 
 
@@ -69,6 +70,12 @@ def prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, val
     check(st, "wgkv_prefill_admit")
     past_key_value.local_length = min(L, W)
     bc, bo, cc, ci = sparse_indices_into(g_mask, W, L, 64)
+    if self.prefill_kernel in (sparse_attn_func_wrapper, sparse_attn_func):
+        # fast path: the admitted columns were just packed into contiguous pool pages
+        return sparse_attn_func_pooled(query_states.transpose(1, 2), key_states.transpose(1, 2),
+                                       value_states.transpose(1, 2), bc, bo, cc, ci, past_key_value.block_pool_k,
+                                       past_key_value.block_pool_v, past_key_value.block_table[self.layer_idx],
+                                       W // c.block_size, c.block_size, softmax_scale=self.scaling)
     return self.prefill_kernel(query_states.transpose(1, 2), key_states.transpose(1, 2),
                                value_states.transpose(1, 2), bc, bo, cc, ci, softmax_scale=self.scaling,
                                causal=True, return_softmax_lse=False)

@@ -60,3 +60,43 @@ def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_in
 
 def sparse_attn_func_wrapper(*args, **kwargs):
     return sparse_attn_func(*args, **kwargs)
+
+
+def sparse_attn_func_pooled(q, k, v, block_count, block_offset, column_count, column_index, pool_k, pool_v,
+                            block_table, table_first, page_size, softmax_scale=None, out=None):
+    """``sparse_attn_func`` whose admitted-column keys are read from the paged pool.
+
+    Valid right after the admission compaction of the same mask: the admitted
+    tokens of (b, h) sit in token order in contiguous pool rows starting at
+    ``block_table[b, h, table_first] * page_size``.  ``block_table`` is the
+    layer's (B, Hk, maxb) table.  Same result as :func:`sparse_attn_func`."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (pool_k, "pool_k"), (block_table, "block_table")):
+        require_cuda(t, n)
+    B, L, Hq, D = q.shape
+    Hk = k.shape[2]
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    R = (L + 63) // 64
+    bc = block_count.reshape(-1).to(torch.int32).contiguous()
+    bo = block_offset.reshape(R, -1).to(torch.int32).contiguous()
+    cc = column_count.to(torch.int32).contiguous()
+    ci = column_index.to(torch.int32)
+    if ci.numel() == 0:
+        ci = torch.zeros(B, Hk, 1, 1, dtype=torch.int32, device=q.device)
+    if ci.stride(3) != 1 or ci.stride(0) != Hk * ci.stride(1):
+        ci = ci.contiguous()
+    assert block_table.dim() == 3 and block_table.stride(2) == 1 and block_table.stride(0) == Hk * block_table.stride(1)
+    assert pool_k.is_contiguous() and pool_v.is_contiguous() and pool_k.shape[-1] == D
+    if out is None:
+        out = torch.empty(B, L, Hq, D, dtype=q.dtype, device=q.device)
+    st = lib.wgkv_sparse_prefill_pooled(q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(),
+                                        k.stride(0), k.stride(1), k.stride(2), v.data_ptr(), v.stride(0),
+                                        v.stride(1), v.stride(2), B, L, Hq, Hk, D, bc.data_ptr(), bo.data_ptr(),
+                                        bo.stride(0), cc.data_ptr(), ci.data_ptr(), ci.stride(1),
+                                        float(softmax_scale), out.data_ptr(), out.stride(0), out.stride(1),
+                                        out.stride(2), pool_k.data_ptr(), pool_v.data_ptr(),
+                                        pool_k.numel() // D, block_table.data_ptr(), block_table.stride(1),
+                                        int(table_first), int(page_size), err_word(q.device).data_ptr(),
+                                        stream_ptr(q.device))
+    check(st, "wgkv_sparse_prefill_pooled")
+    return out
