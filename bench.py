@@ -290,6 +290,7 @@ def gpu_arm(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import wgkv
+    from wgkv.dist import max_over_ranks
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     Ly, B, Hk, Hq, D = CFG["layers"], CFG["batch"], CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"]
@@ -351,10 +352,7 @@ def gpu_arm(args, rank, world, local_rank):
     clocks = clk.stop() if clk else None
     wgkv.check_errors()
     glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = max_over_ranks(ms, dev)
     ms_step = ms / args.steps
     value = world * B * args.steps / (ms / 1e3)
     bytes_step, _ = algorithmic_bytes(cache, (glen_start + glen_end) / 2.0)
@@ -382,10 +380,7 @@ def gpu_arm(args, rank, world, local_rank):
     e3.record()
     torch.cuda.synchronize()
     barrier()
-    te = torch.tensor([e2.elapsed_time(e3)], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = world * B * e_steps / (float(te.item()) / 1e3)
+    e2e = world * B * e_steps / (max_over_ranks(e2.elapsed_time(e3), dev) / 1e3)
     wgkv.check_errors()
 
     # ---- roofline of the dominant kernel (paged decode), timed alone ----
@@ -531,14 +526,24 @@ def prefill_arm(args, rank, world, local_rank):
             idx0 = idx
     torch.cuda.synchronize()
     out = torch.empty_like(q)
-    wgkv.sparse_attn_func(q, kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk], *idx0, softmax_scale=D ** -0.5, out=out)
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record()
-    wgkv.sparse_attn_func(q, kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk], *idx0, softmax_scale=D ** -0.5, out=out)
-    e3.record()
-    torch.cuda.synchronize()
-    attn_ms = e2.elapsed_time(e3)
+    kk, vv = kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk]
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        fn()
+        a1.record()
+        torch.cuda.synchronize()
+        return a0.elapsed_time(a1)
+
+    # the product path: admitted columns from layer 0's compacted pool (same mask as idx0)
+    attn_ms = timed(lambda: wgkv.sparse_attn_func_pooled(q, kk, vv, *idx0, cache.block_pool_k, cache.block_pool_v,
+                                                         cache.block_table[0], W // T, T, softmax_scale=D ** -0.5,
+                                                         out=out))
+    # the generic sparse_attn_func (columns gathered by index from k / v)
+    gather_ms = timed(lambda: wgkv.sparse_attn_func(q, kk, vv, *idx0, softmax_scale=D ** -0.5, out=out))
     f0 = useful_flops(idx0[2].cpu().numpy(), L, W, D, G)
     tf = f0 / (attn_ms / 1e3) / 1e12
     try:
@@ -552,7 +557,8 @@ def prefill_arm(args, rank, world, local_rank):
                        "seq_len": L},
             "admitted_frac": admitted / (Ly * Hk * max(L - W, 1)),
             "useful_tflops_total": flops / 1e12, "tflops_step": flops / (ms / 1e3) / 1e12,
-            "roofline": {"bound": "tensor", "kernel": "sparse_prefill_kernel", "achieved": tf, "peak": pk_tf[0],
+            "sparse_attn_func_gather_ms": gather_ms,
+            "roofline": {"bound": "tensor", "kernel": "sparse_prefill_tc_kernel (pooled)", "achieved": tf, "peak": pk_tf[0],
                          "peak_kind": pk_tf[1], "unit": "TFLOP/s", "frac": tf / pk_tf[0], "traffic": None,
                          "ms_per_launch": attn_ms, "flops_per_launch": f0},
             "gpu_launches": launches, "clocks": clocks}

@@ -22,7 +22,7 @@ from .layers import (  # noqa: F401
     self_attn_forward_patch_inference,
 )
 from .pool import WgkvPool, init_pool  # noqa: F401
-from .prefill import sparse_attn_func, sparse_attn_func_wrapper  # noqa: F401
+from .prefill import sparse_attn_func, sparse_attn_func_pooled, sparse_attn_func_wrapper  # noqa: F401
 from .runtime import check_errors  # noqa: F401
 
 
