@@ -151,6 +151,22 @@ WGKV_API int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos
                                 int64_t v_sb, int64_t v_sh, const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh,
                                 int32_t* cache_seqlens, void* stream);
 
+/*
+ * Decode step without deferred gating, fused: the write gate on the new token of every (b, h)
+ * (same MLP, inputs and rounding as wgkv_gate_scores) writes its admission bit into ring slot
+ * `insert_pos` of local_is_global, k_new / v_new go into that ring slot, and cache_seqlens is
+ * filled as in wgkv_decode_append -- one launch (reference: the gate call in
+ * self_attn_forward_patch :1579 + decode_wrapper :1390-1400, :1429-1432).  Gate inputs are the
+ * (B, Hk, D) rows pre_k_new / k_new / v_new selected by input_mask (bit 0 pre_k, 1 post_k = k_new,
+ * 2 v = v_new).  Run the layer-0 promotion (wgkv_promote) before this, as it reads the old bit.
+ */
+WGKV_API int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                     const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh, const uint16_t* k_new,
+                                     int64_t k_sb, int64_t k_sh, const uint16_t* v_new, int64_t v_sb, int64_t v_sh,
+                                     int input_mask, const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
+                                     const uint16_t* b2, const uint16_t* norm_w, float rms_eps, int inner, int act,
+                                     float threshold, int32_t* cache_seqlens, void* stream);
+
 /* ---- (a9-a11) vertical-slash sparse indices -------------------------------- */
 /*
  * generate_sparse_indices (:385-409) on the device.  Outputs (R = ceil(L / block), P = min(W/block, R)):

@@ -238,3 +238,32 @@ def test_pooled_prefill_matches_gather(wgkv, B, Hk, G, D):
     torch.cuda.synchronize()
     wgkv.check_errors()
     assert torch.equal(pooled, gathered)
+
+
+@pytest.mark.parametrize("inputs,rms,act,inner", [(["pre_k"], False, "gelu", 64), (["pre_k", "post_k"], True, "gelu", 512),
+                                                   (["post_k", "v"], False, "silu", 192)])
+def test_fused_decode_gate_matches_gate_kernel(wgkv, inputs, rms, act, inner):
+    """wgkv_decode_gate_append writes the same admission bits / ring rows as the gate kernel + append."""
+    from types import SimpleNamespace
+    B, Hk, D, W, T = 6, 4, 128, 64, 16
+    torch.manual_seed(0)
+    gp = wgkv.GatingPredictor(D, Hk, inputs, act, inner / D, 1e-3, rms, True).cuda().bfloat16()
+    if rms:
+        with torch.no_grad():
+            gp.pre_key_norm.weight.add_(0.1 * torch.randn_like(gp.pre_key_norm.weight))
+    cache = SimpleNamespace()
+    wgkv.init_pool(cache, layers=2, batch=B, kv_heads=Hk, head_dim=D, window=W, page=T, max_total_tokens=8192,
+                   max_tokens_per_head=1024, device="cuda")
+    mism = 0
+    for step in range(20):
+        pk, k, v = (torch.randn(B, 1, Hk, D, device="cuda").bfloat16().transpose(1, 2) for _ in range(3))
+        ref = torch.empty(B, Hk, 1, dtype=torch.uint8, device="cuda")
+        gp.admit(pk, k, v, 0.5, ref)
+        ins = step % W
+        gp.decode_admit_append(cache, 1, ins, 7, pk, k, v, 0.5)
+        torch.cuda.synchronize()
+        mism += int((cache.local_is_global[1, :, :, ins] != ref[:, :, 0]).sum())
+        rows = cache.block_pool_k[:2 * B * Hk * W].view(2, B, Hk, W, D)[1, :, :, ins]
+        assert torch.equal(rows, k[:, :, 0])
+        assert torch.equal(cache.cache_seqlens, torch.full((B, Hk), 7, dtype=torch.int32, device="cuda"))
+    assert mism <= 1, mism  # accumulation order differs; a bit may flip only at an exact bf16 tie

@@ -334,82 +334,163 @@ __global__ void __launch_bounds__(256) decode_append_kernel(PoolArgs pa, int lay
 // ============================================================================
 // lazy promotion (migrate_local_kv_to_global)
 // ============================================================================
-__global__ void __launch_bounds__(1024) promote_kernel(PoolArgs pa, int ptr) {
+constexpr int kPromoteThreads = 1024;
+constexpr int kPromoteMaxPer = 32;  // (layer, b, h) entries per thread: up to 32768 heads per pool
+
+__global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, int ptr) {
   const wgkv_pool& P = pa.P;
   const int N = P.layers * P.batch * P.kv_heads;
   const int W = P.window, T = P.page, D = P.head_dim;
-  __shared__ int s_cnt, s_ovf, s_nf;
-  __shared__ int wsum[32];
-  if (threadIdx.x == 0) { s_cnt = 0; s_ovf = 0; }
-  __syncthreads();
-  int cnt = 0, ovf = 0;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    if (P.local_is_global[int64_t(i) * W + ptr]) {
-      const int gl = P.global_lengths[i];
-      if (W + gl + 1 > P.max_tokens_per_head) ovf = 1;
-      cnt += (gl % T) == 0;
+  const int per = (N + kPromoteThreads - 1) / kPromoteThreads;
+  const int i0 = threadIdx.x * per;  // contiguous entries keep the (layer, b, h) allocation order
+  __shared__ int wsum[kPromoteThreads / 32];
+  __shared__ int s_ovf, s_nf, s_ok;
+  if (threadIdx.x == 0) s_ovf = 0;
+  // all loads of this thread's entries are issued together; admission bits kept as a bitmask
+  uint32_t fmask = 0;
+#pragma unroll
+  for (int k = 0; k < kPromoteMaxPer; ++k)
+    if (k < per && i0 + k < N && P.local_is_global[int64_t(i0 + k) * W + ptr]) fmask |= 1u << k;
+  int need = 0, ovf = 0;
+#pragma unroll
+  for (int k = 0; k < kPromoteMaxPer; ++k) {
+    if (fmask & (1u << k)) {
+      const int gl = P.global_lengths[i0 + k];
+      need += (gl % T) == 0;
+      ovf |= (W + gl + 1 > P.max_tokens_per_head);
     }
   }
-  atomicAdd(&s_cnt, cnt);
+  // block-wide exclusive scan of `need` (thread order = entry order)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = need;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffff, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
   if (ovf) atomicOr(&s_ovf, 1);
   __syncthreads();
+  int wb = 0, tot = 0;
+  for (int w = 0; w < kPromoteThreads / 32; ++w) {
+    if (w < warp) wb += wsum[w];
+    tot += wsum[w];
+  }
   if (threadIdx.x == 0) {
     const int nf = *P.next_free_block;
     s_nf = nf;
+    s_ok = 0;
     if (s_ovf) {
       set_error(P.err, WGKV_ERR_HEAD_CAPACITY);
-      s_ovf = 1;
-    } else if (int64_t(nf) + s_cnt > P.total_blocks) {
+    } else if (int64_t(nf) + tot > P.total_blocks) {
       set_error(P.err, WGKV_ERR_POOL_EXHAUSTED);
-      s_ovf = 1;
     } else {
-      *P.next_free_block = nf + s_cnt;
+      *P.next_free_block = nf + tot;
+      s_ok = 1;
     }
   }
   __syncthreads();
-  if (s_ovf) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int carry = s_nf;
-  for (int base = 0; base < N; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    int flag = 0, gl = 0;
-    if (i < N) {
-      flag = P.local_is_global[int64_t(i) * W + ptr];
-      if (flag) gl = P.global_lengths[i];
+  if (!s_ok) return;
+  int next = s_nf + wb + x - need;
+#pragma unroll 1
+  for (int k = 0; k < kPromoteMaxPer; ++k) {
+    if (!(fmask & (1u << k))) continue;
+    const int i = i0 + k;
+    const int gl = P.global_lengths[i];
+    int32_t* trow = P.block_table + int64_t(i) * P.max_blocks_per_head + W / T;
+    int pid;
+    if (gl % T == 0) {
+      pid = next++;
+      trow[gl / T] = pid;
+    } else {
+      pid = trow[gl / T];
     }
-    const int need = flag && (gl % T) == 0;
-    // block exclusive scan of `need` in (layer, b, h) order
-    int x = need;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffff, x, o);
-      if (lane >= o) x += y;
+    const int64_t dst = int64_t(pid) * T + gl % T;
+    const int64_t src = int64_t(i) * W + ptr;
+    const uint4* ks = reinterpret_cast<const uint4*>(P.k + src * D);
+    const uint4* vs = reinterpret_cast<const uint4*>(P.v + src * D);
+    uint4* kd = reinterpret_cast<uint4*>(P.k + dst * D);
+    uint4* vd = reinterpret_cast<uint4*>(P.v + dst * D);
+    for (int c = 0; c < D / 8; ++c) {
+      kd[c] = ks[c];
+      vd[c] = vs[c];
     }
-    if (lane == 31) wsum[warp] = x;
-    __syncthreads();
-    int wb = 0, tot = 0;
-    for (int w = 0; w < nw; ++w) {
-      if (w < warp) wb += wsum[w];
-      tot += wsum[w];
+    P.global_lengths[i] = gl + 1;
+  }
+}
+
+// ============================================================================
+// decode: gate on the new key + ring append + cache_seqlens, one CTA per (b, h)
+// ============================================================================
+constexpr int kDgaThreads = 128;
+
+struct DecodeGateParams {
+  RowSrc in[3];  // selected gate inputs (concat order), token stride unused
+  const uint16_t* norm[3];
+  int n_in, I, inner, act;
+  const uint16_t *w1, *b1, *w2, *b2;
+  float eps, thr;
+};
+
+__global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArgs pa, DecodeGateParams g, int layer,
+                                                                          int ins, int cur, RowSrc K, RowSrc V,
+                                                                          int32_t* cache_seqlens) {
+  const wgkv_pool& P = pa.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
+  const int i = blockIdx.x, b = i / Hk, h = i - b * Hk;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float xs[384];
+  __shared__ float part[kDgaThreads / 32];
+  // ---- gate input row(s): one warp per input, optional RMS norm, rounded to bf16 ----
+  if (warp < g.n_in) {
+    const uint16_t* src = g.in[warp].p + b * g.in[warp].sb + h * g.in[warp].sh;
+    const int per = D / 32;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < per) x[j] = bf2f(src[lane * per + j]);
+    if (g.norm[warp]) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += x[j] * x[j];
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+      const float inv = 1.f / sqrtf(ss / float(D) + g.eps);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < per) x[j] = bf16_round(bf2f(g.norm[warp][lane * per + j]) * bf16_round(x[j] * inv));
     }
-    __syncthreads();
-    if (flag) {
-      int32_t* trow = P.block_table + int64_t(i) * P.max_blocks_per_head + W / T;
-      int pid;
-      if (need) {
-        pid = carry + wb + x - need;
-        trow[gl / T] = pid;
-      } else {
-        pid = trow[gl / T];
-      }
-      const int64_t dst = int64_t(pid) * T + gl % T;
-      const int64_t src = int64_t(i) * W + ptr;
-      for (int c = 0; c < D / 8; ++c) {
-        reinterpret_cast<uint4*>(P.k + dst * D)[c] = reinterpret_cast<const uint4*>(P.k + src * D)[c];
-        reinterpret_cast<uint4*>(P.v + dst * D)[c] = reinterpret_cast<const uint4*>(P.v + src * D)[c];
-      }
-      P.global_lengths[i] = gl + 1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < per) xs[warp * D + lane * per + j] = x[j];
+  }
+  // ---- ring append (independent of the gate) ----
+  const int64_t row = (int64_t(layer) * BH + i) * P.window + ins;
+  copy_row<false>(P.k + row * D, K.p + b * K.sb + h * K.sh, D, tid, kDgaThreads);
+  copy_row<false>(P.v + row * D, V.p + b * V.sb + h * V.sh, D, tid, kDgaThreads);
+  if (tid == 0 && cache_seqlens) cache_seqlens[i] = cur + P.global_lengths[layer * BH + i];
+  __syncthreads();
+  // ---- hidden layer: a warp per neuron, lanes over input pairs ----
+  const uint16_t* w1h = g.w1 + int64_t(h) * g.inner * g.I;
+  float acc_out = 0.f;
+  for (int j = warp; j < g.inner; j += kDgaThreads / 32) {
+    const uint32_t* wr = reinterpret_cast<const uint32_t*>(w1h + int64_t(j) * g.I);
+    float s = 0.f;
+    for (int c = lane; c < g.I / 2; c += 32) {
+      const uint32_t w = __ldg(wr + c);
+      s = fmaf(xs[2 * c], __uint_as_float(w << 16), s);
+      s = fmaf(xs[2 * c + 1], __uint_as_float(w & 0xffff0000u), s);
     }
-    carry += tot;
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
+    const float hb = bf16_round(bf16_round(s) + bf2f(g.b1[h * g.inner + j]));
+    acc_out += bf16_round(act_fn(hb, g.act)) * bf2f(g.w2[h * g.inner + j]);
+  }
+  if (lane == 0) part[warp] = acc_out;
+  __syncthreads();
+  if (tid == 0) {
+    float o = 0.f;
+    for (int w = 0; w < kDgaThreads / 32; ++w) o += part[w];
+    o = bf16_round(bf16_round(o) + bf2f(g.b2[h]));
+    const float sc = bf16_round(1.f / (1.f + expf(-o)));
+    P.local_is_global[row] = sc > g.thr ? 1 : 0;  // ring slot `ins` of (layer, b, h)
   }
 }
 
@@ -542,7 +623,8 @@ extern "C" int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len,
 extern "C" int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream) {
   if (!pool_ok(pool) || local_ptr < 0 || local_ptr >= pool->window) return WGKV_EINVAL;
   PoolArgs pa{*pool};
-  promote_kernel<<<1, 1024, 0, as_stream(stream)>>>(pa, local_ptr);
+  if (pool->layers * pool->batch * pool->kv_heads > kPromoteThreads * kPromoteMaxPer) return WGKV_EINVAL;
+  promote_kernel<<<1, kPromoteThreads, 0, as_stream(stream)>>>(pa, local_ptr);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -561,5 +643,47 @@ extern "C" int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_p
   RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0}, PK{pre_k_new, pk_sb, pk_sh, 0};
   decode_append_kernel<<<(BH + 7) / 8, 256, 0, as_stream(stream)>>>(pa, layer, insert_pos, cur_local_len, K, V, PK,
                                                                     cache_seqlens);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                       const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh,
+                                       const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
+                                       int64_t v_sb, int64_t v_sh, int input_mask, const uint16_t* w1,
+                                       const uint16_t* b1, const uint16_t* w2, const uint16_t* b2,
+                                       const uint16_t* norm_w, float rms_eps, int inner, int act, float threshold,
+                                       int32_t* cache_seqlens, void* stream) {
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || insert_pos < 0 || insert_pos >= pool->window ||
+      !k_new || !v_new || !w1 || !b1 || !w2 || !b2 || inner <= 0 || (act != 0 && act != 1))
+    return WGKV_EINVAL;
+  if (((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+        reinterpret_cast<uintptr_t>(pre_k_new) | reinterpret_cast<uintptr_t>(w1)) & 3) ||
+      ((k_sb | k_sh | v_sb | v_sh | pk_sb | pk_sh) & 1))
+    return WGKV_EINVAL;
+  const int D = pool->head_dim;
+  DecodeGateParams g = {};
+  const uint16_t* src[3] = {pre_k_new, k_new, v_new};
+  const int64_t sbs[3] = {pk_sb, k_sb, v_sb}, shs[3] = {pk_sh, k_sh, v_sh};
+  int n = 0;
+  for (int s = 0; s < 3; ++s) {
+    if (!(input_mask & (1 << s))) continue;
+    if (!src[s]) return WGKV_EINVAL;
+    g.in[n] = RowSrc{src[s], sbs[s], shs[s], 0};
+    g.norm[n] = norm_w ? norm_w + s * D : nullptr;
+    ++n;
+  }
+  if (n == 0 || n * D > 384 || (n * D) % 2) return WGKV_EINVAL;
+  g.n_in = n;
+  g.I = n * D;
+  g.inner = inner;
+  g.act = act;
+  g.w1 = w1; g.b1 = b1; g.w2 = w2; g.b2 = b2;
+  g.eps = rms_eps;
+  g.thr = threshold;
+  PoolArgs pa{*pool};
+  RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0};
+  const int BH = pool->batch * pool->kv_heads;
+  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, layer, insert_pos, cur_local_len, K, V,
+                                                                       cache_seqlens);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

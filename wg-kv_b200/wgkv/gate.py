@@ -17,6 +17,7 @@ import torch.nn as nn
 
 from ._lib import check, lib
 from .runtime import require_cuda, stream_ptr
+from .pool import pool_ref
 
 _SLOTS = ("pre_k", "post_k", "v")
 
@@ -123,3 +124,25 @@ class GatingPredictor(nn.Module):
         """Write ``gate(x) > threshold`` (uint8) into ``mask`` (any (B, Hk, L) view); optionally the scores."""
         self._launch(pre_key, post_key, value, threshold, scores, mask)
         return mask
+
+    def decode_admit_append(self, cache, layer, insert_pos, cur_local_len, pre_key, post_key, value, threshold):
+        """Fused decode prologue (``wgkv_decode_gate_append``): gate the new token of every (b, h),
+        write its admission bit and its K/V into ring slot ``insert_pos`` of ``layer``, and fill
+        ``cache.cache_seqlens``.  Inputs are (B, Hk, 1, D) (or (B, Hk, D)) bf16 views."""
+        def rows(t):
+            if t is None:
+                return None, 0, 0
+            t = t[:, :, 0] if t.dim() == 4 else t
+            assert t.stride(2) == 1
+            return t.data_ptr(), t.stride(0), t.stride(1)
+        pk = rows(pre_key if "pre_k" in self.g_inputs else None)
+        kk = rows(post_key)
+        vv = rows(value)
+        w1, b1, w2, b2 = (_bf16(x) for x in (self.conv1.weight, self.conv1.bias, self.conv2.weight, self.conv2.bias))
+        nw = self._norm_weights(post_key.device)
+        st = lib.wgkv_decode_gate_append(pool_ref(cache), layer, insert_pos, cur_local_len, *pk, *kk, *vv,
+                                         self.input_mask, w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
+                                         nw.data_ptr() if nw is not None else None, self._eps(), self.inner_dim,
+                                         self.act, float(threshold), cache.cache_seqlens.data_ptr(),
+                                         stream_ptr(post_key.device))
+        check(st, "wgkv_decode_gate_append")

@@ -100,7 +100,7 @@ def refresh_local_is_global(self, past_key_value, device):
 
 
 def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, g_mask,
-                   local_blocks_per_head):
+                   local_blocks_per_head, appended=False):
     """Ring append + (deferred) admission + ragged paged attention for one token (:1379-1449).
 
     ``g_mask`` (B, Hk, 1): the new token's admission bit, or None when it was
@@ -115,15 +115,8 @@ def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, valu
         insert_pos = past_key_value.local_ptr
         cur = W
     defer = past_key_value.local_pre_key is not None
-    k1 = key_states[:, :, 0]
-    v1 = value_states[:, :, 0]
-    p1 = pre_key[:, :, 0] if (defer and pre_key is not None) else None
-    st = lib.wgkv_decode_append(pool_ref(past_key_value), l, insert_pos, cur, k1.data_ptr(), k1.stride(0),
-                                k1.stride(1), v1.data_ptr(), v1.stride(0), v1.stride(1),
-                                p1.data_ptr() if p1 is not None else None, p1.stride(0) if p1 is not None else 0,
-                                p1.stride(1) if p1 is not None else 0, past_key_value.cache_seqlens.data_ptr(),
-                                stream_ptr(device))
-    check(st, "wgkv_decode_append")
+    if not appended:
+        _append(self, past_key_value, l, insert_pos, cur, pre_key, key_states, value_states, defer, device)
     if g_mask is not None:
         past_key_value.local_is_global[l, :, :, insert_pos] = g_mask[:, :, 0].to(torch.uint8)
     elif defer and insert_pos == W - 1:
@@ -139,6 +132,19 @@ def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, valu
     handle = self.decode_kernel_handle(query_states.transpose(1, 2), k_cache, v_cache, past_key_value.cache_seqlens,
                                        past_key_value.block_table[l], self.scaling)
     return self.decode_kernel_executor(handle)
+
+
+def _append(self, past_key_value, l, insert_pos, cur, pre_key, key_states, value_states, defer, device):
+    """Ring append + cache_seqlens (wgkv_decode_append)."""
+    k1 = key_states[:, :, 0]
+    v1 = value_states[:, :, 0]
+    p1 = pre_key[:, :, 0] if (defer and pre_key is not None) else None
+    st = lib.wgkv_decode_append(pool_ref(past_key_value), l, insert_pos, cur, k1.data_ptr(), k1.stride(0),
+                                k1.stride(1), v1.data_ptr(), v1.stride(0), v1.stride(1),
+                                p1.data_ptr() if p1 is not None else None, p1.stride(0) if p1 is not None else 0,
+                                p1.stride(1) if p1 is not None else 0, past_key_value.cache_seqlens.data_ptr(),
+                                stream_ptr(device))
+    check(st, "wgkv_decode_append")
 
 
 def self_attn_forward_patch_inference(self, past_key_value, input_shape, query_states, pre_key, key_states,
@@ -197,9 +203,13 @@ def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, i
     l = self.layer_idx
     if l == 0 and past_key_value.local_length == W:
         migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
-    insert_pos = past_key_value.local_length if past_key_value.local_length < W else past_key_value.local_ptr
-    self.g_predictors.admit(pre_key, key_states, value_states, c.g_threshold,
-                            past_key_value.local_is_global[l, :, :, insert_pos:insert_pos + 1])
+    if past_key_value.local_length < W:
+        insert_pos, cur = past_key_value.local_length, past_key_value.local_length + 1
+    else:
+        insert_pos, cur = past_key_value.local_ptr, W
+    # one fused launch: gate on the new key -> admission bit in the ring slot, K/V append, cache_seqlens
+    self.g_predictors.decode_admit_append(past_key_value, l, insert_pos, cur, pre_key, key_states, value_states,
+                                          c.g_threshold)
     out = self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, None,
-                              local_blocks_per_head)
+                              local_blocks_per_head, appended=True)
     return out, None, None
