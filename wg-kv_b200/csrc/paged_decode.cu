@@ -27,7 +27,7 @@
 namespace wgkv {
 namespace {
 
-constexpr int kNCW = 4;              // consumer warps
+constexpr int kNCW = 8;  // consumer warps (the kernel is consumer-bound below 8)
 constexpr int kThreads = 32 * (kNCW + 1);
 constexpr int kMaxBH = 4096;          // max batch * kv_heads handled in shared memory
 constexpr int kCtasPerSM = 1;
@@ -49,29 +49,30 @@ struct DecodeParams {
   int* err;
 };
 
-template <int D>
+// D: head dim; S: pipeline stages (3 for D=128 when shared memory allows, else fewer)
+template <int D, int S>
 struct Cfg {
   static constexpr int kUnitBytes = 16 * D * 2;         // one K (or V) unit
   static constexpr int kStageBytes = kNCW * 2 * kUnitBytes;
-  static constexpr int kStages = D == 128 ? 5 : 8;
+  static constexpr int kStages = S;
   static constexpr int kBoxes = D / 64;                 // 64-column TMA boxes per unit
 };
 
-template <int D>
+template <int D, int S>
 size_t smem_bytes(int BH, int G) {
   size_t s = 1024;  // alignment slack
-  s += size_t(Cfg<D>::kStages) * Cfg<D>::kStageBytes;
+  s += size_t(Cfg<D, S>::kStages) * Cfg<D, S>::kStageBytes;
   s += size_t(BH + 1 + 256) * 4;                        // prefix + scan scratch
   s += size_t(kNCW) * G * (D + 2) * 4;                  // cross-warp merge
-  s += 2 * Cfg<D>::kStages * 8 + 64;                    // barriers + flags
+  s += 2 * Cfg<D, S>::kStages * 8 + 64;                 // barriers + flags
   return s;
 }
 
-template <int D>
+template <int D, int S>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         DecodeParams p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D>
+template <int D, int S>
 int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t num_pages, int page_size,
            const int32_t* seqlens, const int32_t* table, int64_t table_stride, int B, int Hq, int Hk, float scale,
            uint16_t* out, void* ws, size_t ws_bytes, int* err, cudaStream_t stream) {
@@ -432,17 +433,17 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t nu
   p.counters = reinterpret_cast<int*>(ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + ((size_t(BH) * 4 + 255) & ~size_t(255)));
   p.err = err;
-  const size_t smem = smem_bytes<D>(BH, G);
+  const size_t smem = smem_bytes<D, S>(BH, G);
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(paged_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+    if (cudaFuncSetAttribute(paged_decode_kernel<D, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
         cudaSuccess)
       return WGKV_ECUDA;
     attr_set[dev] = true;
   }
-  paged_decode_kernel<D><<<grid, kThreads, smem, stream>>>(tmK, tmV, p);
+  paged_decode_kernel<D, S><<<grid, kThreads, smem, stream>>>(tmK, tmV, p);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -468,15 +469,23 @@ extern "C" int wgkv_paged_decode(const uint16_t* q, const uint16_t* k_cache, con
   if (num_q_heads / num_kv_heads > 16 || page_size <= 0 || page_size % 16 != 0 || num_pages <= 0) return WGKV_EINVAL;
   if (batch * num_kv_heads > kMaxBH) return WGKV_EINVAL;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return WGKV_EINVAL;
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const int BH = batch * num_kv_heads, G = num_q_heads / num_kv_heads;
+  const cudaStream_t st = as_stream(stream);
+#define WGKV_DEC_LAUNCH(DD, SS)                                                                                     \
+  launch<DD, SS>(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table, table_stride, batch,         \
+                 num_q_heads, num_kv_heads, softmax_scale, out, workspace, workspace_bytes, err, st)
+  // deepest pipeline that fits next to the prefix and merge buffers
   switch (head_dim) {
     case 64:
-      return launch<64>(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table, table_stride, batch,
-                        num_q_heads, num_kv_heads, softmax_scale, out, workspace, workspace_bytes, err,
-                        as_stream(stream));
+      if (smem_bytes<64, 6>(BH, G) <= kMaxSmem) return WGKV_DEC_LAUNCH(64, 6);
+      if (smem_bytes<64, 3>(BH, G) <= kMaxSmem) return WGKV_DEC_LAUNCH(64, 3);
+      return WGKV_EINVAL;
     case 128:
-      return launch<128>(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table, table_stride, batch,
-                         num_q_heads, num_kv_heads, softmax_scale, out, workspace, workspace_bytes, err,
-                         as_stream(stream));
+      if (smem_bytes<128, 3>(BH, G) <= kMaxSmem) return WGKV_DEC_LAUNCH(128, 3);
+      if (smem_bytes<128, 2>(BH, G) <= kMaxSmem) return WGKV_DEC_LAUNCH(128, 2);
+      return WGKV_EINVAL;
+#undef WGKV_DEC_LAUNCH
     default:
       return WGKV_EINVAL;
   }
