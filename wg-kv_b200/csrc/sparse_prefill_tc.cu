@@ -5,21 +5,26 @@
 // sparse_attn_func computes for generate_sparse_indices' indices, pinned by
 // utils/test_sparse_attn.py:34-93).  One CTA owns one 64-query row block of
 // one KV head and 2*NM query heads of its GQA group, i.e. NM M-tiles of 128
-// rows (two heads x 64 queries each) that share every K/V tile:
+// rows (two heads x 64 queries each) that share every K/V tile.  K/V tiles
+// hold 128 keys (two 64-key halves), so both MMAs run at N >= 128, where a
+// 128-row tcgen05 MMA reaches full rate (at N = 64 it does not):
 //
-//   warp 0      TMA producer: Q once; per 64-key tile, K and V into 3-stage
-//               rings.  Admitted-column tiles are gathered with
-//               cp.async.bulk.tensor tile::gather4 (4 key rows per
-//               instruction, indices from column_index); band tiles are plain
-//               2D tiles.  SWIZZLE_128B, no multicast.
-//   warp 1      TMEM allocator + single-thread MMA issuer:
-//               S_t = Q_t K^T  (M=128, N=64, K=D; S double-buffered in TMEM)
-//               O_t += P_t V   (M=128, N=D, K=64; P from shared memory)
-//   warps 2..   one warpgroup per M-tile: reads S rows from TMEM (one row per
-//               thread), masks (column tail / causal band), online softmax in
-//               base 2 with a lazy running max (O is rescaled in TMEM only when
-//               the max grows by more than 2^8), writes P as bf16 into the
-//               canonical K-major SW128 layout, and finally normalises O.
+//   warp 0      TMA producer: Q once; per tile, K and V into 2-stage rings.
+//               Admitted-column halves are gathered with tile::gather4 (four
+//               key rows per instruction, from column_index) or, in pooled
+//               mode, loaded as contiguous rows of the compacted pool; band
+//               halves are plain 2D tiles.  SWIZZLE_128B, no multicast.
+//   warp 1      TMEM allocator + single-thread MMA issuer, per M-tile t:
+//               S_t = Q_t K^T (M=128, N=128, K=D, A/B in shared memory), then,
+//               once the softmax has written P_t into the S columns,
+//               O_t += P_t V (M=128, N=D, K=128, A = P from TMEM).  The two
+//               M-tiles alternate, so one tile's softmax overlaps the other's MMAs.
+//   warps 2..   two warpgroups per M-tile, one per 64-key half: each thread owns
+//               one row of its half (TMEM lane = row); masks (column tail /
+//               causal band), swaps the tile's row max with its partner half,
+//               online softmax in base 2 with a lazy running max (O rescaled in
+//               TMEM only when the max grows by more than 2^8), writes P as
+//               packed bf16 into TMEM, and finally normalises its half of O.
 #include "common.cuh"
 #include "runtime.h"
 #include "tc.cuh"
@@ -27,23 +32,22 @@
 namespace wgkv {
 namespace {
 
-constexpr int kKeys = 64;  // keys per K/V tile
-constexpr int kKS = 3;     // K stages
-constexpr int kVS = 3;     // V stages
+constexpr int kKeys = 128;  // keys per K/V tile (two 64-key halves)
+constexpr int kStg = 2;     // K and V stages
 constexpr float kRescaleThreshold = 8.f;  // log2 of the largest tolerated growth of unnormalised terms
 
 template <int D, int NM>
 struct Tc {
-  static constexpr int kDB = D / 64;               // 64-column boxes per row
-  static constexpr int kQTile = kDB * 16384;       // one M-tile of Q: kDB boxes x 128 rows x 128 B
-  static constexpr int kKV = kDB * kKeys * 128;    // one K or V stage
-  static constexpr int kP = 128 * 128;             // 128 rows x 64 keys x 2 B
+  static constexpr int kDB = D / 64;                 // 64-column boxes per row
+  static constexpr int kQTile = kDB * 16384;         // one M-tile of Q: kDB boxes x 128 rows x 128 B
+  static constexpr int kBox = kKeys * 128;           // one 64-column box of a K/V tile (128 rows x 128 B)
+  static constexpr int kKV = kDB * kBox;             // one K or V stage
   static constexpr int kOffK = NM * kQTile;
-  static constexpr int kOffV = kOffK + kKS * kKV;
-  static constexpr int kOffP = kOffV + kVS * kKV;
-  static constexpr int kOffBar = kOffP + NM * kP;
-  static constexpr int kSmem = kOffBar + 512 + 1024;  // barriers + alignment slack
-  static constexpr int kThreads = 64 + 128 * NM;
+  static constexpr int kOffV = kOffK + kStg * kKV;
+  static constexpr int kOffBar = kOffV + kStg * kKV;
+  static constexpr int kOffX = kOffBar + 512;        // row-max / row-sum exchange [3][NM][2][128] floats
+  static constexpr int kSmem = kOffX + 3 * NM * 2 * 128 * 4 + 1024;  // + alignment slack
+  static constexpr int kThreads = 64 + 256 * NM;     // producer, MMA, two softmax warpgroups per M-tile
   static constexpr int kTmemCols = NM == 2 ? 512 : 256;
 };
 
@@ -71,10 +75,9 @@ struct TcParams {
 
 struct Bars {
   uint64_t qfull;
-  uint64_t kfull[kKS], kempty[kKS];
-  uint64_t vfull[kVS], vempty[kVS];
-  uint64_t sfull[2][2], sfree[2][2];
-  uint64_t pfull[2], odone[2];
+  uint64_t kfull[kStg], kempty[kStg];
+  uint64_t vfull[kStg], vempty[kStg];
+  uint64_t sfull[2], pfull[2], odone[2];
   uint32_t tmem;
 };
 
@@ -97,18 +100,23 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
   const int s0 = i * 64;
   const int hq0 = h * p.G + hg * 2 * NM;  // first query head of this CTA
   const int ncol = p.cc[(int64_t(b) * p.Hk + h) * p.R + i];
-  const int nband = p.bc[i];
+  const int nband = p.bc[i];               // 64-key band blocks
   const int ntc = (ncol + kKeys - 1) / kKeys;
-  const int n = ntc + nband;
+  const int ntb = (nband + 1) / 2;         // band tiles: block pairs (2m, 2m+1)
+  const int n = ntc + ntb;
   const int32_t* bo_row = p.bo + int64_t(i) * p.bo_stride;
 
   if (tid == 0) {
     mbar_init(&bar->qfull, 1);
-    for (int s = 0; s < kKS; ++s) { mbar_init(&bar->kfull[s], 1); mbar_init(&bar->kempty[s], 1); }
-    for (int s = 0; s < kVS; ++s) { mbar_init(&bar->vfull[s], 1); mbar_init(&bar->vempty[s], 1); }
+    for (int s = 0; s < kStg; ++s) {
+      mbar_init(&bar->kfull[s], 1);
+      mbar_init(&bar->kempty[s], 1);
+      mbar_init(&bar->vfull[s], 1);
+      mbar_init(&bar->vempty[s], 1);
+    }
     for (int t = 0; t < 2; ++t) {
-      for (int u = 0; u < 2; ++u) { mbar_init(&bar->sfull[t][u], 1); mbar_init(&bar->sfree[t][u], 4); }
-      mbar_init(&bar->pfull[t], 4);
+      mbar_init(&bar->sfull[t], 1);
+      mbar_init(&bar->pfull[t], 8);
       mbar_init(&bar->odone[t], 1);
     }
     fence_barrier_init();
@@ -140,19 +148,16 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
                         (hq0 + 2 * t + hh) * D + d * 64, b * p.L + s0);
     }
     const int32_t* cib = p.ci + (int64_t(b) * p.Hk + h) * p.ci_stride;
-    // lane -> (4-row group, 64-column box) of a gathered tile
-    const int grp = C::kDB == 2 ? (lane & 15) : lane;
-    const int dl = C::kDB == 2 ? (lane >> 4) : 0;
-    // gather indices are fetched two tiles ahead so their latency hides behind the stage waits
     const int pool_row0 =
         POOL && ncol > 0 ? __ldg(p.table + (int64_t(b) * p.Hk + h) * p.t_stride + p.t_first) * p.t_page : 0;
+    // gathered column tiles: lane -> 4-row group `grp` of the 128 rows, both 64-column boxes
+    // (D = 128: lanes 0-31 cover rows 0..127 of box 0 and then box 1)
     auto fetch = [&](int j, int* r4) {
-      // pooled mode gathers only the partial last column tile (full tiles are contiguous pool rows;
-      // rows past a head's admitted count may hold anything, so they are not read)
-      if (j < ntc && (!POOL || ncol - j * kKeys < kKeys) && grp < 16) {
+      const bool gath = j < ntc && (!POOL || ncol - j * kKeys < kKeys);
+      if (gath) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          int e = j * kKeys + grp * 4 + r;
+          int e = j * kKeys + lane * 4 + r;
           e = e < ncol ? e : ncol - 1;  // past the tail: any valid row (masked in the softmax)
           r4[r] = __ldg(cib + e);
         }
@@ -163,6 +168,7 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
     fetch(1, pre1);
     for (int j = 0; j < n && ok; ++j) {
       const bool col = j < ntc;
+      const bool pooled = POOL && col && ncol - j * kKeys >= kKeys;
       int rows4[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
@@ -170,28 +176,36 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
         pre0[r] = pre1[r];
       }
       fetch(j + 2, pre1);
-      const int off = col ? (POOL ? pool_row0 + j * kKeys : 0) : __ldg(bo_row + (j - ntc));
+      int off0 = 0, off1 = -1;  // row coordinates of the two 64-key halves
+      if (pooled) {
+        off0 = pool_row0 + j * kKeys;
+        off1 = off0 + 64;
+      } else if (!col) {
+        const int m = j - ntc;
+        off0 = b * p.L + __ldg(bo_row + 2 * m);
+        off1 = 2 * m + 1 < nband ? b * p.L + __ldg(bo_row + 2 * m + 1) : off0;  // a missing half is masked
+      }
+      const int s = j % kStg;
+      const uint32_t ph = (j / kStg) & 1;
       for (int kv = 0; kv < 2; ++kv) {
-        const int nst = kv ? kVS : kKS;
-        const int s = j % nst;
-        const uint32_t ph = (j / nst) & 1;
         uint64_t* full = kv ? &bar->vfull[s] : &bar->kfull[s];
         uint64_t* empty = kv ? &bar->vempty[s] : &bar->kempty[s];
         if (!mbar_wait(empty, ph ^ 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
         uint8_t* st = sm + (kv ? C::kOffV : C::kOffK) + s * C::kKV;
         if (lane == 0) mbar_arrive_expect_tx(full, C::kKV);
         __syncwarp();
-        if (POOL && col && ncol - j * kKeys >= kKeys) {
-          // a full tile of compacted admitted columns: 64 contiguous pool rows
-          if (lane == 0)
-            for (int d = 0; d < C::kDB; ++d) tma_load_2d(st + d * 8192, kv ? &tmVp : &tmKp, full, d * 64, off);
-        } else if (col) {
-          if (grp < 16)
-            tma_gather4(st + dl * 8192 + grp * 512, kv ? &tmVg : &tmKg, full, h * D + dl * 64, rows4[0], rows4[1],
+        if (col && !pooled) {
+#pragma unroll
+          for (int d = 0; d < C::kDB; ++d)
+            tma_gather4(st + d * C::kBox + lane * 512, kv ? &tmVg : &tmKg, full, h * D + d * 64, rows4[0], rows4[1],
                         rows4[2], rows4[3]);
         } else if (lane == 0) {
-          for (int d = 0; d < C::kDB; ++d)
-            tma_load_2d(st + d * 8192, kv ? &tmV : &tmK, full, h * D + d * 64, b * p.L + off);
+          const CUtensorMap* m = pooled ? (kv ? &tmVp : &tmKp) : (kv ? &tmV : &tmK);
+          const int x0 = pooled ? 0 : h * D;
+          for (int d = 0; d < C::kDB; ++d) {
+            tma_load_2d(st + d * C::kBox, m, full, x0 + d * 64, off0);
+            tma_load_2d(st + d * C::kBox + 8192, m, full, x0 + d * 64, off1);
+          }
         }
         __syncwarp();
       }
@@ -203,89 +217,95 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
       const uint32_t id_pv = umma_idesc_bf16(128, D, 0, 1);
       if (!mbar_wait(&bar->qfull, 0)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
       for (int j = 0; j <= n && ok; ++j) {
-        if (j < n) {
-          const int ks = j % kKS;
-          if (!mbar_wait(&bar->kfull[ks], (j / kKS) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
-          const uint32_t kst = smem_u32(sm + C::kOffK + ks * C::kKV);
-          const int sb = j & 1;
-          for (int t = 0; t < NM; ++t) {
-            if (!mbar_wait(&bar->sfree[t][sb], ((j >> 1) & 1) ^ 1)) {
-              set_error(p.err, WGKV_ERR_TIMEOUT);
-              ok = false;
-              break;
-            }
+        const int s = j % kStg, ps = (j - 1) % kStg;
+        if (j < n && !mbar_wait(&bar->kfull[s], (j / kStg) & 1)) {
+          set_error(p.err, WGKV_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        if (j > 0 && !mbar_wait(&bar->vfull[ps], ((j - 1) / kStg) & 1)) {
+          set_error(p.err, WGKV_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        const uint32_t kst = smem_u32(sm + C::kOffK + s * C::kKV);
+        const uint32_t vst = smem_u32(sm + C::kOffV + ps * C::kKV);
+        for (int t = 0; t < NM; ++t) {
+          const uint32_t tS = tmem + t * 256, tO = tS + 128;
+          if (j > 0) {
+            // O_t += P_t(j-1) V(j-1): P sits as packed bf16 pairs in S_t's first 64 columns
+            if (!mbar_wait(&bar->pfull[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
             tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < kKeys / 16; ++k) {
+              const uint64_t bb = umma_desc_sw128(vst + k * 2048, C::kBox, 1024);
+              umma_ts(tO, tS + k * 8, bb, id_pv, (j > 1 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&bar->odone[t]);
+          }
+          if (j < n) {
+            // S_t = Q_t K(j)^T; issued after PV_t(j-1), which read P from these columns
             const uint32_t qt = smem_u32(sm + t * C::kQTile);
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
               const uint64_t a = umma_desc_sw128(qt + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
-              const uint64_t bb = umma_desc_sw128(kst + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024);
-              umma_ss(tmem + t * 256 + sb * 64, a, bb, id_qk, k > 0 ? 1u : 0u);
+              const uint64_t bb = umma_desc_sw128(kst + (k >> 2) * C::kBox + (k & 3) * 32, 16, 1024);
+              umma_ss(tS, a, bb, id_qk, k > 0 ? 1u : 0u);
             }
-            umma_commit(&bar->sfull[t][sb]);
+            umma_commit(&bar->sfull[t]);
           }
-          if (!ok) break;
-          umma_commit(&bar->kempty[ks]);
         }
-        if (j > 0) {
-          const int jj = j - 1;
-          const int vs = jj % kVS;
-          if (!mbar_wait(&bar->vfull[vs], (jj / kVS) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
-          const uint32_t vst = smem_u32(sm + C::kOffV + vs * C::kKV);
-          for (int t = 0; t < NM; ++t) {
-            if (!mbar_wait(&bar->pfull[t], jj & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
-            tc_fence_after();
-            const uint32_t pt = smem_u32(sm + C::kOffP + t * C::kP);
-#pragma unroll
-            for (int k = 0; k < kKeys / 16; ++k) {
-              const uint64_t a = umma_desc_sw128(pt + k * 32, 16, 1024);
-              const uint64_t bb = umma_desc_sw128(vst + k * 2048, 8192, 1024);
-              umma_ss(tmem + t * 256 + 128, a, bb, id_pv, (jj > 0 || k > 0) ? 1u : 0u);
-            }
-            umma_commit(&bar->odone[t]);
-          }
-          if (!ok) break;
-          umma_commit(&bar->vempty[vs]);
-        }
+        if (!ok) break;
+        if (j > 0) umma_commit(&bar->vempty[ps]);
+        if (j < n) umma_commit(&bar->kempty[s]);
       }
     }
     __syncwarp();
   } else {
     // ============================ softmax warpgroups ============================
-    const int t = (warp - 2) >> 2;
+    const int sw = warp - 2;
+    const int t = sw >> 3;
+    const int half = (sw >> 2) & 1;           // 64-key half of every tile
     const int quad = warp & 3;
     const int row = quad * 32 + lane;         // TMEM lane = row of M-tile t
     const int hh = 2 * t + (row >> 6);
     const int q = s0 + (row & 63);
+    const int bar_id = 1 + t * 4 + quad;       // named barrier of the two warps sharing these rows
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
-    uint8_t* prow = sm + C::kOffP + t * C::kP + row * 128;
+    float* xm = reinterpret_cast<float*>(sm + C::kOffX);  // [slot][t][half][row]
+    auto xslot = [&](int slot, int hf) { return xm + ((slot * NM + t) * 2 + hf) * 128 + row; };
     const float sc = p.scale_log2;
+    constexpr int kOC = D / 2;                 // O columns of this warpgroup
     float m_used = -INFINITY, l = 0.f;
-    for (int j = 0; j < n && ok; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&bar->sfull[t][sb], (j >> 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+    for (int j = 0; j < n; ++j) {
+      if (ok && !mbar_wait(&bar->sfull[t], j & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
       tc_fence_after();
       float sv[64];
-      tmem_ld32(trow + sb * 64, sv);
-      tmem_ld32(trow + sb * 64 + 32, sv + 32);
+      tmem_ld32(trow + half * 64, sv);
+      tmem_ld32(trow + half * 64 + 32, sv + 32);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->sfree[t][sb]);
       // mask (raw scores; the positive scale is applied inside the exponent) + tile max
       float mraw = -INFINITY;
-      if (j < ntc && ncol - j * kKeys >= kKeys) {  // full admitted-column tile: nothing to mask
+      int lim;
+      if (j < ntc) {
+        lim = ncol - j * kKeys - half * 64 - 1;  // column tail
+      } else {
+        const int blk = 2 * (j - ntc) + half;
+        lim = blk < nband ? min(q, p.L - 1) - __ldg(bo_row + blk) : -1;  // causal band / missing block
+      }
+      if (lim >= 63) {
 #pragma unroll
         for (int c = 0; c < 64; c += 2) mraw = fmaxf(mraw, fmaxf(sv[c], sv[c + 1]));
       } else {
-        const int lim = j < ntc ? ncol - j * kKeys - 1                              // column tail
-                                : min(q, p.L - 1) - __ldg(bo_row + (j - ntc));      // causal band
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           sv[c] = c <= lim ? sv[c] : -INFINITY;
           mraw = fmaxf(mraw, sv[c]);
         }
       }
+      *xslot(j & 1, half) = mraw;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");  // both halves have read S_t
+      mraw = fmaxf(mraw, *xslot(j & 1, half ^ 1));
       const float mt = mraw * sc;
       float alpha = 1.f;
       bool need = false;
@@ -304,31 +324,26 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
         sum1 += p1;
         pk[c >> 1] = pack_bf16x2(p0, p1);
       }
-      const float sum = sum0 + sum1;
-      l = l * alpha + sum;
+      l = l * alpha + (sum0 + sum1);
       if (j > 0) {
-        // PV(j-1) must be done before P is overwritten and before O is rescaled
-        if (!mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+        // PV(j-1) completed before S(j) did (commit order), so O is stable here
+        if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
         tc_fence_after();
         if (__any_sync(0xffffffff, need && alpha != 1.f)) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 32) {
+          for (int c0 = 0; c0 < kOC; c0 += 32) {
             float ov[32];
-            tmem_ld32(trow + 128 + c0, ov);
+            tmem_ld32(trow + 128 + half * kOC + c0, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) ov[c] *= alpha;
-            tmem_st32(trow + 128 + c0, ov);
+            tmem_st32(trow + 128 + half * kOC + c0, ov);
           }
-          tmem_wait_st();
         }
       }
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        const uint4 v = make_uint4(pk[c8 * 4], pk[c8 * 4 + 1], pk[c8 * 4 + 2], pk[c8 * 4 + 3]);
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
+      // P -> TMEM: keys 64*half .. +63 as 32 packed columns over S columns both halves have read
+      tmem_st32(trow + half * 32, reinterpret_cast<const float*>(pk));
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->pfull[t]);
@@ -338,13 +353,16 @@ __global__ void __launch_bounds__(Tc<D, NM>::kThreads, 1)
       if (!mbar_wait(&bar->odone[t], (n - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
     }
     tc_fence_after();
+    *xslot(2, half) = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+    l += *xslot(2, half ^ 1);
     const bool any = l > 0.f;  // a row that saw no key (degenerate index sets only) writes zeros
     const float inv = any ? 1.f / l : 0.f;
-    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh;
+    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh + half * kOC;
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
+    for (int c0 = 0; c0 < kOC; c0 += 32) {
       float ov[32];
-      tmem_ld32(trow + 128 + c0, ov);
+      tmem_ld32(trow + 128 + half * kOC + c0, ov);
       tmem_wait_ld();
       if (ok && q < p.L) {
         if (!any) {
