@@ -438,6 +438,8 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
   const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
   const int i = blockIdx.x, b = i / Hk, h = i - b * Hk;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the paged-decode launch that follows may start its set-up now (it waits for this grid's results)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float xs[384];
   __shared__ float part[kDgaThreads / 32];
   // ---- gate input row(s): one warp per input, optional RMS norm, rounded to bf16 ----
@@ -468,21 +470,25 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
   copy_row<false>(P.v + row * D, V.p + b * V.sb + h * V.sh, D, tid, kDgaThreads);
   if (tid == 0 && cache_seqlens) cache_seqlens[i] = cur + P.global_lengths[layer * BH + i];
   __syncthreads();
-  // ---- hidden layer: a warp per neuron, lanes over input pairs ----
+  // ---- hidden layer: a thread per neuron (W1 row read as 16-byte vectors), fp32 dot products ----
   const uint16_t* w1h = g.w1 + int64_t(h) * g.inner * g.I;
   float acc_out = 0.f;
-  for (int j = warp; j < g.inner; j += kDgaThreads / 32) {
-    const uint32_t* wr = reinterpret_cast<const uint32_t*>(w1h + int64_t(j) * g.I);
+  for (int j = tid; j < g.inner; j += kDgaThreads) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w1h + int64_t(j) * g.I);
     float s = 0.f;
-    for (int c = lane; c < g.I / 2; c += 32) {
-      const uint32_t w = __ldg(wr + c);
-      s = fmaf(xs[2 * c], __uint_as_float(w << 16), s);
-      s = fmaf(xs[2 * c + 1], __uint_as_float(w & 0xffff0000u), s);
+    for (int c = 0; c < g.I / 8; ++c) {
+      const uint4 w = __ldg(wr + c);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s = fmaf(xs[c * 8 + 2 * e], __uint_as_float(ww[e] << 16), s);
+        s = fmaf(xs[c * 8 + 2 * e + 1], __uint_as_float(ww[e] & 0xffff0000u), s);
+      }
     }
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
     const float hb = bf16_round(bf16_round(s) + bf2f(g.b1[h * g.inner + j]));
     acc_out += bf16_round(act_fn(hb, g.act)) * bf2f(g.w2[h * g.inner + j]);
   }
+  for (int o = 16; o; o >>= 1) acc_out += __shfl_xor_sync(0xffffffff, acc_out, o);
   if (lane == 0) part[warp] = acc_out;
   __syncthreads();
   if (tid == 0) {
@@ -672,7 +678,7 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
     g.norm[n] = norm_w ? norm_w + s * D : nullptr;
     ++n;
   }
-  if (n == 0 || n * D > 384 || (n * D) % 2) return WGKV_EINVAL;
+  if (n == 0 || n * D > 384 || (n * D) % 8 || (reinterpret_cast<uintptr_t>(w1) & 15)) return WGKV_EINVAL;
   g.n_in = n;
   g.I = n * D;
   g.inner = inner;

@@ -62,7 +62,7 @@ template <int D, int S>
 size_t smem_bytes(int BH, int G) {
   size_t s = 1024;  // alignment slack
   s += size_t(Cfg<D, S>::kStages) * Cfg<D, S>::kStageBytes;
-  s += size_t(BH + 1 + 256) * 4;                        // prefix + scan scratch
+  s += size_t(BH + 1 + kThreads) * 4;                   // prefix + scan scratch
   s += size_t(kNCW) * G * (D + 2) * 4;                  // cross-warp merge
   s += 2 * Cfg<D, S>::kStages * 8 + 64;                 // barriers + flags
   return s;
@@ -77,8 +77,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
   int* pre = reinterpret_cast<int*>(smem + C::kStages * C::kStageBytes);
-  int* scan = pre + p.BH + 1;  // 256 ints
-  float* merge = reinterpret_cast<float*>(scan + 256);
+  int* scan = pre + p.BH + 1;  // kThreads ints
+  float* merge = reinterpret_cast<float*>(scan + kThreads);
   const int G = p.G;
   uint64_t* full = reinterpret_cast<uint64_t*>(merge + kNCW * G * (D + 2) + 1);
   full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
@@ -89,6 +89,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int BH = p.BH;
+
+  // Inputs (lengths, tables, queries, ring rows) may be written by the kernel launched just before
+  // this one (programmatic dependent launch lets this grid start early): wait for it before reading.
+  if (tid == 0) {
+    for (int st = 0; st < C::kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kNCW);
+    }
+    fence_barrier_init();
+  }
+  if (tid == 32) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- prefix sum of 16-token units per (b, h) ---------------------------
   {
@@ -112,13 +127,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = i0; i < i1; ++i) {
       pre[i] = run;
       run += (max(p.seqlens[i], 0) + 15) >> 4;
-    }
-    if (tid == 0) {
-      for (int s = 0; s < C::kStages; ++s) {
-        mbar_init(&full[s], 1);
-        mbar_init(&empty[s], kNCW);
-      }
-      fence_barrier_init();
     }
     __syncthreads();
   }
@@ -443,7 +451,17 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t nu
       return WGKV_ECUDA;
     attr_set[dev] = true;
   }
-  paged_decode_kernel<D, S><<<grid, kThreads, smem, stream>>>(tmK, tmV, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap set-up with the prior kernel
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<D, S>, tmK, tmV, p) != cudaSuccess) return WGKV_ECUDA;
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
