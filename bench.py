@@ -38,6 +38,18 @@ sys.path.insert(0, os.path.join(HERE, "wg-kv_b200"))
 CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=16, ctx=131072, q_heads=32, kv_heads=8, head_dim=128,
            window=4096, page=16, admit="Beta(2,8)", gate="pre_k->64->1 GELU sigmoid", threshold=0.5)
 METRIC = "decode tok/s @128K ragged cache (Llama-8B shape, B=16, 32 layers)"
+# Qwen3-4B-shaped decode, batch 64, per-sequence context uniform in 8K..32K,
+# ring 2048, aggressive gating (per-head admit ~ Beta(1,10))
+QWEN3_CFG = dict(model="Qwen3-4B-shaped", layers=36, batch=64, ctx=32768, ctx_min=8192, q_heads=32, kv_heads=8,
+                 head_dim=128, window=2048, page=16, admit="Beta(1,10)", gate="pre_k->64->1 GELU sigmoid",
+                 threshold=0.5)
+WORKLOAD_NAME = "C2 decode: Llama-3.1-8B shape, B=16/GPU, 128K ctx, W=4096, T=16, Beta(2,8) admit"
+QWEN3_METRIC = "decode tok/s @8-32K mixed ragged cache (Qwen3-4B shape, B=64, 36 layers)"
+
+
+def _admit_params():
+    a = CFG["admit"]
+    return tuple(float(x) for x in a[a.index("(") + 1:a.index(")")].split(","))
 
 
 def peaks():
@@ -54,9 +66,13 @@ def peaks():
 # ----------------------------------------------------------------------------
 
 def draw_lengths(seed, Ly, B, Hk, ctx, W):
+    """Per-(layer, sequence, head) admit rates and global lengths; per-sequence contexts are uniform in
+    [ctx_min, ctx] when the workload sets ctx_min."""
     rng = np.random.default_rng(seed)
-    rate = rng.beta(2, 8, (Ly, B, Hk))
-    glen = np.round(rate * (ctx - W)).astype(np.int64)
+    a, b = _admit_params()
+    rate = rng.beta(a, b, (Ly, B, Hk))
+    ctx_b = rng.integers(CFG["ctx_min"], ctx + 1, B) if "ctx_min" in CFG else np.full(B, ctx)
+    glen = np.round(rate * (ctx_b[None, :, None] - W)).astype(np.int64)
     return rate, glen
 
 
@@ -236,7 +252,7 @@ def cpu_sample_step(seed=5):
         O.paged_decode(q, kc, vc, sl, bt, D ** -0.5)
         st.local_length = W  # keep the ring full for the next sample
     desc = (f"1 sequence x 1 layer of the decode step (8 KV heads, {int((W + glen).sum())} cached tokens, "
-            f"gate+promote+append+attention), numpy oracle; tok/s = 1 / (t_sample x 32 layers)")
+            f"gate+promote+append+attention), numpy oracle; tok/s = 1 / (t_sample x {CFG["layers"]} layers)")
     return run, desc
 
 
@@ -276,7 +292,7 @@ def reference_arm(args, rank, world):
     line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "C2 decode (one step sample: 1 sequence x 1 layer)", **CFG},
+            "config": {"workload": WORKLOAD_NAME + " (one step sample: 1 sequence x 1 layer)", **CFG},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -426,8 +442,8 @@ def gpu_arm(args, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C2 decode: Llama-3.1-8B shape, B=16/GPU, 128K ctx, W=4096, T=16, Beta(2,8) admit",
-                       "l2": "inputs larger than L2 (~62 GB cache), no flush", "parallelism": f"dp{world} (sequences)",
+            "config": {"workload": WORKLOAD_NAME,
+                       "l2": f"inputs larger than L2 ({cache.block_pool_k.numel() * 4 / 1e9:.0f} GB cache), no flush", "parallelism": f"dp{world} (sequences)",
                        **CFG},
             "hbm_gbs_step": bytes_step / (ms_step / 1e3) / 1e9,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int((inputs[0][..., Hq:].numel() + qbuf[0].numel()) * 2),
@@ -572,10 +588,17 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode"])
     ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
     args = ap.parse_args()
-    if args.small and args.workload == "decode":
+    global METRIC, WORKLOAD_NAME
+    if args.workload == "qwen3_decode":
+        CFG.clear()
+        CFG.update(QWEN3_CFG)
+        METRIC = QWEN3_METRIC
+        WORKLOAD_NAME = ("C4 decode: Qwen3-4B shape, B=64/GPU, ctx U[8K,32K] per sequence, W=2048, T=16, "
+                         "Beta(1,10) admit")
+    if args.small and args.workload != "prefill":
         CFG["layers"] = 2
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -355,9 +355,40 @@ def regen_decode_inputs(params):
     return q, kc, vc, seqlens, table
 
 
+def gate_checkpoint_case(m):
+    """A 2-layer gate checkpoint in the reference's save format (scripts/train.py:311-335: the
+    trainable parameters, keys model.layers.{i}.self_attn.g_predictors.*) and the reference's fast-path
+    scores for seeded inputs.  Small shapes (D=64, 2 KV heads, pre_k + post_k, RMS, expand 1.5)."""
+    torch.manual_seed(7)
+    out = {}
+    rng = np.random.default_rng(77)
+    D, Hk, L = 64, 2, 40
+    for layer in range(2):
+        gp = m.GatingPredictor(D, Hk, ["pre_k", "post_k"], "gelu", 1.5, 1e-3, True, True)
+        with torch.no_grad():
+            gp.pre_key_norm.weight.add_(0.1 * torch.randn(D))
+            gp.post_key_norm.weight.add_(0.1 * torch.randn(D))
+        gp = gp.to(torch.bfloat16)
+        for k_, v_ in gp.state_dict().items():
+            out[f"model.layers.{layer}.self_attn.g_predictors.{k_}"] = O.bf16_bits(v_.float().numpy())
+        pk = O.randn_bf16(rng, (1, Hk, L, D))
+        kk = O.randn_bf16(rng, (1, Hk, L, D))
+        with torch.no_grad():
+            sc = gp(tb(pk), tb(kk), None)
+        out[f"scores_{layer}"] = O.bf16_bits(nb(sc))
+        out[f"pre_k_{layer}"] = O.bf16_bits(pk)
+        out[f"post_k_{layer}"] = O.bf16_bits(kk)
+    np.savez_compressed(os.path.join(HERE, "gate_ckpt.npz"), **out)
+    print("gate_ckpt written")
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 1)
     m, t = load_reference()
+    if os.environ.get("WGKV_GOLDEN_ONLY") == "gate_ckpt":
+        gate_checkpoint_case(m)
+        return
+    gate_checkpoint_case(m)
     decode_cases(t)
     indices_cases(m)
     # C1: the CPU-reference single-layer configuration (32 q / 8 kv heads,

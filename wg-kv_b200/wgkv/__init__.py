@@ -11,7 +11,7 @@ from .decode import (  # noqa: F401
     flash_attn_with_kvcache_wrapper_triton_handle,
     paged_decode,
 )
-from .gate import GatingPredictor, GatingRMSNorm  # noqa: F401
+from .gate import GatingPredictor, GatingRMSNorm, load_gate_checkpoint  # noqa: F401
 from .indices import generate_sparse_indices, sparse_indices_into  # noqa: F401
 from .layers import (  # noqa: F401
     decode_wrapper,

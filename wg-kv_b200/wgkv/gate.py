@@ -146,3 +146,32 @@ class GatingPredictor(nn.Module):
                                          self.act, float(threshold), cache.cache_seqlens.data_ptr(),
                                          stream_ptr(post_key.device))
         check(st, "wgkv_decode_gate_append")
+
+
+def load_gate_checkpoint(modules, state, prefix="model.layers.{i}.self_attn.g_predictors.", strict=True):
+    """Load a WG-KV gate checkpoint into per-layer gates.
+
+    ``state`` is the dict the reference's training script saves (``scripts/train.py:311-335``:
+    ``{name: param}`` of the trainable parameters, loaded with ``load_state_dict(strict=False)`` at
+    ``scripts/profiling.py:223-226``) or a path to it.  ``modules[i]`` is layer i's attention module
+    (anything with ``.g_predictors``) or its :class:`GatingPredictor`.  Returns the keys used."""
+    if isinstance(state, str):
+        state = torch.load(state, map_location="cpu", weights_only=True)
+    used = []
+    for i, m in enumerate(modules):
+        gp = m.g_predictors if hasattr(m, "g_predictors") else m
+        pre = prefix.format(i=i)
+        sub = {k[len(pre):]: torch.as_tensor(v) for k, v in state.items() if k.startswith(pre)}
+        if not sub:
+            if strict:
+                raise KeyError(f"no gate parameters under {pre!r}")
+            continue
+        own = gp.state_dict()
+        for k, v in sub.items():
+            if k not in own:
+                raise KeyError(f"unexpected gate parameter {pre + k}")
+            if tuple(own[k].shape) != tuple(v.shape):
+                raise ValueError(f"{pre + k}: shape {tuple(v.shape)} != {tuple(own[k].shape)}")
+        gp.load_state_dict({k: v.to(own[k].dtype) for k, v in sub.items()}, strict=strict)
+        used += [pre + k for k in sub]
+    return used
