@@ -434,6 +434,18 @@ def gpu_arm(args, rank, world, local_rank):
         except Exception:
             traffic = None
 
+    cache_gb = cache.block_pool_k.numel() * 4 / 1e9
+    h2d_step = int((inputs[0][..., Hq:].numel() + qbuf[0].numel()) * 2)
+    d2h_step = int(outbuf.numel() * 2)
+    prefill = None
+    if world == 1 and args.workload == "decode" and not args.no_prefill and not args.small:
+        # the 400K sparse prefill on the same GPU, decode cache released first
+        del cache, layers, inputs, qbuf, outbuf, outs, host_in, host_q, dev_in, dev_q, host_out
+        torch.cuda.empty_cache()
+        pl = prefill_arm(args, rank, world, local_rank, emit=False)
+        prefill = {k: pl[k] for k in ("metric", "value", "unit", "admitted_frac", "tflops_step", "roofline",
+                                      "sparse_attn_func_gather_ms", "gpu_launches", "clocks")}
+        prefill["workload"] = pl["config"]["workload"]
     if rank == 0:
         cpu_val, cpu_desc = (None, None)
         if world == 1:
@@ -443,17 +455,19 @@ def gpu_arm(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD_NAME,
-                       "l2": f"inputs larger than L2 ({cache.block_pool_k.numel() * 4 / 1e9:.0f} GB cache), no flush", "parallelism": f"dp{world} (sequences)",
+                       "l2": f"inputs larger than L2 ({cache_gb:.0f} GB cache), no flush", "parallelism": f"dp{world} (sequences)",
                        **CFG},
             "hbm_gbs_step": bytes_step / (ms_step / 1e3) / 1e9,
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int((inputs[0][..., Hq:].numel() + qbuf[0].numel()) * 2),
-                    "d2h_bytes_per_step": int(outbuf.numel() * 2)},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d_step,
+                    "d2h_bytes_per_step": d2h_step},
             "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "bytes_per_launch": kbytes, "ms_per_launch": per_launch_ms},
             "gpu_launches": launches,
             "clocks": clocks,
         }
+        if prefill is not None:
+            line["prefill_400k"] = prefill
         if cpu_val is not None:
             line["cpu_baseline"] = {"value": cpu_val, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
                                     "sample": cpu_desc}
@@ -479,7 +493,7 @@ def useful_flops(cc, L, W, D, G, blk=64):
     return 4.0 * D * G * (float(pairs.sum()) + B * Hk * float(band.sum()))
 
 
-def prefill_arm(args, rank, world, local_rank):
+def prefill_arm(args, rank, world, local_rank, emit=True):
     import torch
     import wgkv
     dev = torch.device("cuda", local_rank)
@@ -578,8 +592,9 @@ def prefill_arm(args, rank, world, local_rank):
                          "peak_kind": pk_tf[1], "unit": "TFLOP/s", "frac": tf / pk_tf[0], "traffic": None,
                          "ms_per_launch": attn_ms, "flops_per_launch": f0},
             "gpu_launches": launches, "clocks": clocks}
-    if rank == 0:
+    if rank == 0 and emit:
         print(json.dumps(line), flush=True)
+    return line
 
 
 def main():
@@ -590,6 +605,7 @@ def main():
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode"])
     ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the 400K prefill measurement of the default run")
     args = ap.parse_args()
     global METRIC, WORKLOAD_NAME
     if args.workload == "qwen3_decode":
