@@ -229,6 +229,19 @@ WGKV_API int wgkv_sparse_prefill_pooled(const uint16_t* q, int64_t q_sb, int64_t
                                         const int32_t* table, int64_t table_stride, int table_first, int page_size,
                                         int* err, void* stream);
 
+/*
+ * Helper of the generic sparse_attn_func path: copies, for every (b, h), the K/V rows
+ * column_index[b, h, 0 : column_count[b, h, R-1]) (the admitted columns the last row block uses,
+ * which include every other row block's) into contiguous rows (b*Hk + h)*cap + c of out_k / out_v
+ * ((B*Hk*cap, D) bf16, cap >= that count).  wgkv_sparse_prefill_pooled with a page table of
+ * (b*Hk + h)*cap (page size 1) then reads them as plain 2D tiles.  No reference counterpart: the
+ * reference gathers inside its (vLLM fork) kernel.
+ */
+WGKV_API int wgkv_gather_columns(const uint16_t* k, int64_t k_sb, int64_t k_sl, int64_t k_sh, const uint16_t* v,
+                                 int64_t v_sb, int64_t v_sl, int64_t v_sh, int batch, int num_kv_heads, int head_dim,
+                                 int seq_len, const int32_t* column_count, const int32_t* column_index,
+                                 int64_t ci_stride, int64_t cap, uint16_t* out_k, uint16_t* out_v, void* stream);
+
 /* ---- (a7, a8) ragged paged decode attention ----------------------------- */
 /*
  * out[b, 0, hq, :] = softmax(q[b, 0, hq, :] . K_h^T * scale) V_h, h = hq / G,

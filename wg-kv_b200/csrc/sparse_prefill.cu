@@ -307,3 +307,59 @@ extern "C" int wgkv_sparse_prefill_pooled(const uint16_t* q, int64_t q_sb, int64
                              num_q_heads, num_kv_heads, head_dim, block_count, block_offset, bo_stride, column_count,
                              column_index, ci_stride, softmax_scale, out, o_sb, o_sl, o_sh, err, stream);
 }
+
+// ----------------------------------------------------------------------------
+// Admitted-column compaction for the generic sparse_attn_func path: copies the
+// K/V rows column_index[b, h, 0 : column_count[b, h, R-1]) of every (b, h) into
+// contiguous scratch rows (b*Hk + h) * cap + c, so the tensor-core kernel reads
+// them as plain 2D TMA tiles (the same layout the paged pool has after prefill
+// compaction).  HBM-bound: one read and one write per admitted row.
+// ----------------------------------------------------------------------------
+namespace wgkv {
+namespace {
+constexpr int kGatherRows = 32;  // rows per CTA (256 threads, 8 lanes per row)
+
+__global__ void __launch_bounds__(256) gather_columns_kernel(const uint16_t* k, int64_t k_sb, int64_t k_sl,
+                                                             int64_t k_sh, const uint16_t* v, int64_t v_sb,
+                                                             int64_t v_sl, int64_t v_sh, int Hk, int D, int R,
+                                                             const int32_t* cc, const int32_t* ci,
+                                                             int64_t ci_stride, int64_t cap, uint16_t* dk,
+                                                             uint16_t* dv) {
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk;
+  const int64_t last = cc[int64_t(bh) * R + R - 1];
+  const int count = int(last < cap ? last : cap);
+  const int r = blockIdx.x * kGatherRows + (threadIdx.x >> 3);
+  const int lane8 = threadIdx.x & 7;
+  if (r >= count) return;
+  const int t = ci[int64_t(bh) * ci_stride + r];
+  const uint4* sk = reinterpret_cast<const uint4*>(k + b * k_sb + int64_t(t) * k_sl + h * k_sh);
+  const uint4* sv = reinterpret_cast<const uint4*>(v + b * v_sb + int64_t(t) * v_sl + h * v_sh);
+  uint4* ok = reinterpret_cast<uint4*>(dk + (int64_t(bh) * cap + r) * D);
+  uint4* ov = reinterpret_cast<uint4*>(dv + (int64_t(bh) * cap + r) * D);
+  for (int c = lane8; c < D / 8; c += 8) {
+    ok[c] = __ldg(sk + c);
+    ov[c] = __ldg(sv + c);
+  }
+}
+}  // namespace
+}  // namespace wgkv
+
+extern "C" int wgkv_gather_columns(const uint16_t* k, int64_t k_sb, int64_t k_sl, int64_t k_sh, const uint16_t* v,
+                                   int64_t v_sb, int64_t v_sl, int64_t v_sh, int batch, int num_kv_heads,
+                                   int head_dim, int seq_len, const int32_t* column_count,
+                                   const int32_t* column_index, int64_t ci_stride, int64_t cap, uint16_t* out_k,
+                                   uint16_t* out_v, void* stream) {
+  using namespace wgkv;
+  if (!k || !v || !column_count || !column_index || !out_k || !out_v || batch <= 0 || num_kv_heads <= 0 ||
+      seq_len <= 0 || cap <= 0 || (head_dim != 64 && head_dim != 128))
+    return WGKV_EINVAL;
+  if (((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out_k) |
+        reinterpret_cast<uintptr_t>(out_v)) & 15) || ((k_sb | k_sl | k_sh | v_sb | v_sl | v_sh) % 8))
+    return WGKV_EINVAL;
+  const int R = (seq_len + 63) / 64;
+  dim3 grid((cap + kGatherRows - 1) / kGatherRows, batch * num_kv_heads);
+  gather_columns_kernel<<<grid, 256, 0, as_stream(stream)>>>(k, k_sb, k_sl, k_sh, v, v_sb, v_sl, v_sh, num_kv_heads,
+                                                             head_dim, R, column_count, column_index, ci_stride, cap,
+                                                             out_k, out_v);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}

@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from ._lib import check, lib
-from .runtime import err_word, require_cuda, stream_ptr
+from .runtime import err_word, require_cuda, stream_ptr, workspace
 
 
 def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_index, softmax_scale=None,
@@ -49,6 +49,19 @@ def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_in
         ci = ci.contiguous()
     if out is None:
         out = torch.empty(B, L, Hq, D, dtype=q.dtype, device=q.device)
+    cap = ci.shape[3]
+    if _tc_eligible(q, k, v, out) and B * Hk * cap < 2 ** 31:
+        # compact the admitted columns into contiguous rows, then read them as plain TMA tiles
+        ws = workspace(q.device, "columns", 2 * B * Hk * cap * D * 2)
+        ck = ws[:B * Hk * cap * D * 2].view(torch.bfloat16).view(B * Hk * cap, D)
+        cv = ws[B * Hk * cap * D * 2:2 * B * Hk * cap * D * 2].view(torch.bfloat16).view(B * Hk * cap, D)
+        st = lib.wgkv_gather_columns(k.data_ptr(), k.stride(0), k.stride(1), k.stride(2), v.data_ptr(), v.stride(0),
+                                     v.stride(1), v.stride(2), B, Hk, D, L, cc.data_ptr(), ci.data_ptr(), ci.stride(1),
+                                     cap, ck.data_ptr(), cv.data_ptr(), stream_ptr(q.device))
+        check(st, "wgkv_gather_columns")
+        base = (torch.arange(B * Hk, dtype=torch.int32, device=q.device) * cap).view(B, Hk, 1)
+        return sparse_attn_func_pooled(q, k, v, block_count, block_offset, cc, ci, ck, cv, base, 0, 1,
+                                       softmax_scale=softmax_scale, out=out)
     st = lib.wgkv_sparse_prefill(q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(), k.stride(0),
                                  k.stride(1), k.stride(2), v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), B, L,
                                  Hq, Hk, D, bc.data_ptr(), bo.data_ptr(), bo.stride(0), cc.data_ptr(), ci.data_ptr(),
@@ -56,6 +69,18 @@ def sparse_attn_func(q, k, v, block_count, block_offset, column_count, column_in
                                  out.stride(2), err_word(q.device).data_ptr(), stream_ptr(q.device))
     check(st, "wgkv_sparse_prefill")
     return out
+
+
+def _tc_eligible(q, k, v, out):
+    """Shapes the tensor-core kernel takes (mirrors the check in sparse_prefill_tc.cu)."""
+    B, L, Hq, D = q.shape
+    Hk = k.shape[2]
+    if (Hq // Hk) % 2 or D not in (64, 128):
+        return False
+    for t in (q, k, v):
+        if t.stride(2) != D or t.stride(1) % 8 or (B > 1 and t.stride(0) != L * t.stride(1)) or t.data_ptr() % 16:
+            return False
+    return out.data_ptr() % 16 == 0 and all(x % 8 == 0 for x in out.stride()[:3])
 
 
 def sparse_attn_func_wrapper(*args, **kwargs):
