@@ -597,13 +597,126 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
     return line
 
 
+# ----------------------------------------------------------------------------
+# Llama-8B decode, batch 64 at 256K context, KV heads sharded across GPUs
+# (8 -> 8/N per GPU, each GPU its own paged pool), row-parallel o_proj + NCCL all-reduce per layer.
+# ----------------------------------------------------------------------------
+C5_CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=64, ctx=262144, q_heads=32, kv_heads=8, head_dim=128,
+              window=4096, page=16, admit="Beta(2,8)", gate="pre_k->64->1 GELU sigmoid", threshold=0.5, hidden=4096)
+
+
+def c5_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import wgkv
+    from wgkv.dist import kv_head_shard, max_over_ranks
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    Ly, B, D, W, T = C5_CFG["layers"], C5_CFG["batch"], C5_CFG["head_dim"], C5_CFG["window"], C5_CFG["page"]
+    (h0, h1), (q0, q1) = kv_head_shard(C5_CFG["kv_heads"], C5_CFG["q_heads"], rank, world)
+    Hk, Hq = h1 - h0, q1 - q0
+    # resident layer pools: all 32 when they fit in ~150 GB, else as many as fit, cycled over the 32 layers
+    CFG.clear()
+    CFG.update(C5_CFG)
+    CFG["kv_heads"], CFG["q_heads"] = Hk, Hq
+    _, glen = draw_lengths(2 + 1000 * rank, 1, B, Hk, C5_CFG["ctx"], W)
+    per_layer = float(((W + glen) * D * 2 * 2).sum()) * 1.02
+    resident = int(max(1, min(Ly, 150e9 // per_layer)))
+    CFG["layers"] = resident
+    steps_total = args.warmup + args.steps + 8
+    cache, rate, glen0 = build_state(dev, steps_total * ((Ly + resident - 1) // resident), seed=2 + 1000 * rank)
+    layers = build_layers(dev, rate, seed=3 + 1000 * rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    NI = 4
+    inputs = torch.randn(NI, Ly, B, 1, Hq + 3 * Hk, D, generator=g, device=dev).to(torch.bfloat16)
+    qbuf = inputs[..., :Hq, :].contiguous()
+    hidden = C5_CFG["hidden"]
+    wo = (torch.randn(hidden, Hq * D, generator=g, device=dev) * (Hq * D * world) ** -0.5).to(torch.bfloat16)
+    y = torch.empty(B, hidden, dtype=torch.bfloat16, device=dev)
+
+    def step(s):
+        for l in range(Ly):
+            a = layers[l % resident]
+            x = inputs[s % NI, l]
+            q = qbuf[s % NI, l].transpose(1, 2)
+            k = x[:, :, Hq:Hq + Hk].transpose(1, 2)
+            v = x[:, :, Hq + Hk:Hq + 2 * Hk].transpose(1, 2)
+            pk = x[:, :, Hq + 2 * Hk:].transpose(1, 2)
+            o, _, _ = a.self_attn_forward_patch(a, 3, None, cache, (B, 1), q, pk, k, v)
+            # row-parallel o_proj on this GPU's heads, summed over GPUs (the only exchange)
+            torch.matmul(o.view(B, Hq * D), wo.t(), out=y)
+            if world > 1:
+                dist.all_reduce(y)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    glen_start = cache.global_lengths.cpu().numpy().astype(np.int64)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(args.steps):
+        step(s)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.stop() if clk else None
+    ms = max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
+    wgkv.check_errors()
+    glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
+    # per-GPU attention bytes per step (32 layer visits over the resident pools)
+    sl = W + (glen_start + glen_end) / 2.0
+    visits = np.bincount(np.arange(Ly) % resident, minlength=resident)
+    attn_bytes = float((sl.sum(axis=(1, 2)) * visits).sum()) * D * 2 * 2
+    kc = cache.block_pool_k.view(cache.total_blocks, T, D)
+    vc = cache.block_pool_v.view(cache.total_blocks, T, D)
+    seq0 = (cache.global_lengths[0] + W).to(torch.int32).contiguous()
+    od = torch.empty(B, 1, Hq, D, dtype=torch.bfloat16, device=dev)
+    qd = qbuf[0, 0].contiguous()
+    wgkv.paged_decode(qd, kc, vc, seq0, cache.block_table[0], D ** -0.5, out=od)
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(5):
+        wgkv.paged_decode(qd, kc, vc, seq0, cache.block_table[0], D ** -0.5, out=od)
+    e3.record()
+    torch.cuda.synchronize()
+    kms = e2.elapsed_time(e3) / 5
+    kbytes = float(seq0.sum().item()) * D * 2 * 2
+    peak, peak_kind = peaks()
+    ach = kbytes / (kms / 1e3) / 1e9
+    if rank == 0:
+        line = {"metric": "decode tok/s @256K ragged cache, KV heads sharded (Llama-8B shape, B=64, 32 layers)",
+                "value": B / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
+                           "resident_layer_pools": resident,
+                           "note": ("all 32 layer pools resident" if resident == Ly else
+                                    f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
+                           "parallelism": f"tp{world} (KV heads)", **C5_CFG},
+                "per_gpu_tok_s": B / (ms / 1e3) / world,
+                "attn_hbm_gbs_per_gpu": attn_bytes / (ms / 1e3) / 1e9,
+                "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": ach, "peak": peak,
+                             "peak_kind": peak_kind, "unit": "GB/s", "frac": ach / peak, "ms_per_launch": kms,
+                             "bytes_per_launch": kbytes},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode", "c5_decode"])
     ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 400K prefill measurement of the default run")
     args = ap.parse_args()
@@ -630,6 +743,8 @@ def main():
     try:
         if args.workload == "prefill":
             prefill_arm(args, rank, world, local_rank)
+        elif args.workload == "c5_decode":
+            c5_arm(args, rank, world, local_rank)
         else:
             gpu_arm(args, rank, world, local_rank)
     finally:
