@@ -710,13 +710,126 @@ def c5_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def model_arm(args, rank, world, local_rank):
+    """TTFT / TPOT of a whole random-init decoder on the WG-KV path (scripts/profiling.py:346-418)."""
+    import torch
+    import wgkv
+    from wgkv.dist import max_over_ranks
+    from wgkv.model import SHAPES, WgkvDecoder
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    shape = SHAPES[args.model]
+    B, P, K, Wu = args.batch, args.prompt, args.steps, args.warmup
+    n_eager = min(K, 32)
+    total = P + Wu + n_eager + 2 * K + 16
+    m = WgkvDecoder(shape, batch=B, window=args.window, max_tokens_per_head=total + args.window + 64,
+                    g_defer=not args.no_defer, max_positions=total, device=dev, seed=rank)
+    m.calibrate_gates()
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    ids = torch.randint(0, shape.vocab, (B, P), generator=g, device=dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def sync_ms(fn):
+        torch.cuda.synchronize()
+        a, b = ev(), ev()
+        a.record()
+        r = fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b), r
+
+    # warm-up: a prefill and decode steps on a throw-away cache (profiling.py:351-362)
+    c = SimpleNamespace()
+    m.prefill(ids, c)
+    for _ in range(Wu):
+        m.decode_step(c)
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    del c
+    # attention / MLP / lm_head breakdown (profiling.py:251-344), eager, on its own cache
+    c = SimpleNamespace()
+    m.timers = {}
+    m.prefill(ids, c)
+    torch.cuda.synchronize()
+    bd_prefill = m.breakdown()
+    m.timers = {}
+    for _ in range(8):
+        m.decode_step(c)
+    torch.cuda.synchronize()
+    bd_decode = {k: v / 8 for k, v in m.breakdown().items()}
+    m.timers = None
+    del c
+    torch.cuda.empty_cache()
+
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    cache = SimpleNamespace()
+    ttft, _ = sync_ms(lambda: m.prefill(ids, cache))
+    l0 = wgkv.lib.launches
+    eager_ms, _ = sync_ms(lambda: [m.decode_step(cache) for _ in range(n_eager)])
+    per_step_launches = (wgkv.lib.launches - l0) // n_eager
+    dg = m.decode_graph(cache)  # one more real step, eager, then captured
+    torch.cuda.synchronize()
+    graph_ms, _ = sync_ms(lambda: [dg.replay() for _ in range(K)])
+    clocks = clk.stop() if clk else None
+    wgkv.check_errors()
+    glen = cache.global_lengths.double().mean().item()
+    D, Hk, Ly = shape.head_dim, shape.kv_heads, shape.layers
+    kv_bytes = B * Ly * Hk * (glen + min(args.window, P)) * 2 * D * 2
+    w_bytes = m.weight_bytes() - m.embed.numel() * 2
+    tpot = max_over_ranks(graph_ms, dev) / K
+    tpot_eager = max_over_ranks(eager_ms, dev) / n_eager
+    ttft = max_over_ranks(ttft, dev)
+
+    # end to end through the public API: each step's token ids come from pinned host memory (teacher
+    # forcing) and each step's greedy token is read back to the host
+    host_tok = torch.randint(0, shape.vocab, (K, B, 1), dtype=torch.int64).pin_memory()
+    out_host = torch.empty(K, B, dtype=torch.int64, pin_memory=True)
+
+    def e2e_run():
+        for s in range(K):
+            m.token.copy_(host_tok[s], non_blocking=True)
+            dg.replay()
+            out_host[s].copy_(m.token[:, 0], non_blocking=True)
+    e2e_ms, _ = sync_ms(e2e_run)
+    e2e_ms = max_over_ranks(e2e_ms, dev)
+    wgkv.check_errors()
+    peak, kind = peaks()
+    achieved = (w_bytes + kv_bytes) / (tpot / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": f"decode tok/s, graph-replayed steps after a {P}-token prefill ({shape.name}, B={B})",
+            "value": world * B / (tpot / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": Wu,
+            "ms_per_step": tpot, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids; random-init weights",
+            "config": {"workload": f"end-to-end decoder ({args.model}), TTFT + TPOT as scripts/profiling.py",
+                       "model": shape.name, "batch": B, "prompt": P, "window": args.window, "page": 16,
+                       "g_defer": not args.no_defer, "admit": "Beta(2,8) per head (calibrated gate bias)",
+                       "l2": "weights + KV larger than L2 each step, no flush"},
+            "ttft_ms": ttft, "prefill_tok_s": B * P / (ttft / 1e3), "tpot_ms_graph": tpot, "tpot_ms_eager": tpot_eager,
+            "breakdown_ms": {"prefill": bd_prefill, "decode_step": bd_decode},
+            "e2e": {"value": world * B * K / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
+                    "d2h_bytes_per_step": B * 8},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + KV read)", "achieved": achieved,
+                         "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                         "bytes_per_step": w_bytes + kv_bytes},
+            "gpu_launches": per_step_launches * K, "clocks": clocks,
+        }
+        print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode", "c5_decode"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode", "c5_decode", "model"])
+    ap.add_argument("--model", default="llama-3.2-1b", help="model workload: llama-3.2-1b | llama-3.1-8b | qwen3-4b")
+    ap.add_argument("--prompt", type=int, default=32000, help="model workload: prompt length")
+    ap.add_argument("--batch", type=int, default=1, help="model workload: sequences")
+    ap.add_argument("--window", type=int, default=4096, help="model workload: local window")
+    ap.add_argument("--no-defer", action="store_true", help="model workload: gate each token at decode")
     ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 400K prefill measurement of the default run")
     args = ap.parse_args()
@@ -745,6 +858,8 @@ def main():
             prefill_arm(args, rank, world, local_rank)
         elif args.workload == "c5_decode":
             c5_arm(args, rank, world, local_rank)
+        elif args.workload == "model":
+            model_arm(args, rank, world, local_rank)
         else:
             gpu_arm(args, rank, world, local_rank)
     finally:

@@ -16,9 +16,12 @@
  *   wgkv_gate_scores          GatingPredictor.forward fast path :170-196 + `g_scores > g_threshold` :1465
  *   wgkv_prefill_admit        prefill_wrapper ring fill + compaction :1290-1331
  *   wgkv_promote              migrate_local_kv_to_global :674-763
+ *   wgkv_ring_advance         local_ptr / local_length update in decode_wrapper :1408-1413
  *   wgkv_decode_append        decode_wrapper ring append / local_is_global :1390-1413, tables :1429-1436
  *   wgkv_decode_gate_append   self_attn_forward_patch gate on one token :1579 fused with the above
- *   wgkv_refresh_ring         refresh_local_is_global :1169-1180 (deferred gating)
+ *   wgkv_decode_prologue      the same, fused behind q/k norm + RoPE (modeling_llama.py:265-271,
+ *                             modeling_qwen3.py:236-239)
+ *   (deferred gating)         refresh_local_is_global :1169-1180 is wgkv_gate_scores over the ring rows
  *   wgkv_sparse_indices       generate_sparse_indices :385-409 (+ generate_block_offset :321-349,
  *                             generate_column_index :352-381)
  *   wgkv_sparse_prefill       sparse_attn_func (vLLM fork) as called at :1366-1374
@@ -51,6 +54,7 @@ extern "C" {
 #define WGKV_ERR_POOL_EXHAUSTED 0x2 /* page allocation past total_blocks */
 #define WGKV_ERR_TIMEOUT 0x4        /* an mbarrier wait gave up (kernel returned early) */
 #define WGKV_ERR_BAD_PAGE 0x8       /* a page id outside [0, total_blocks) was met */
+#define WGKV_ERR_BAD_POSITION 0x10  /* a RoPE position outside the caller's tables (clamped) */
 
 /* Library version and build info. */
 WGKV_API int wgkv_version(void);
@@ -70,6 +74,11 @@ WGKV_API int wgkv_num_sms(void);
  *   local_pre_key    (layers, batch, kv_heads, window, head_dim) bf16, deferred gating only (else NULL)
  *   next_free_block  device int32 scalar: bump allocator of global pages
  *   err              device int32 error word (WGKV_ERR_* bits)
+ *   ring_state       optional device int32[2] = {local_length, local_ptr}: the ring position the
+ *                    reference keeps on the host (:1286-1287, :1408-1413).  When set, the decode entry
+ *                    points accept WGKV_RING_ON_DEVICE in place of insert_pos / local_ptr and read the
+ *                    position here, and wgkv_ring_advance moves it, so that one captured CUDA graph
+ *                    replays every decode step.  NULL = positions come from the host only.
  * The ring slot s of (layer l, batch b, head h) is pool row ((l*batch + b)*kv_heads + h)*window + s.
  */
 typedef struct wgkv_pool {
@@ -90,7 +99,11 @@ typedef struct wgkv_pool {
   int32_t page;
   int32_t max_blocks_per_head;
   int32_t max_tokens_per_head;
+  int32_t* ring_state;
 } wgkv_pool;
+
+/* insert_pos / local_ptr value that means "read the position from pool->ring_state". */
+#define WGKV_RING_ON_DEVICE (-1)
 
 /* ---- (a1, a2) write gate + admission mask --------------------------------- */
 /*
@@ -135,16 +148,25 @@ WGKV_API int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len, c
  * head's global pages (a new page from next_free_block when the length is a multiple of `page`,
  * allocated in (layer, b, h) order) and bump global_lengths.  One launch for all layers, as the
  * reference does at layer 0 when the ring is full (:1470-1471).  Capacity violations write nothing
- * and set err.
+ * and set err.  local_ptr = WGKV_RING_ON_DEVICE: the slot is ring_state[1], and nothing happens while
+ * ring_state[0] < window (the reference promotes only once the ring is full, :1470).
  */
 WGKV_API int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream);
+
+/*
+ * Advance pool->ring_state by one decoded token, as decode_wrapper does after the last layer
+ * (:1408-1413): local_length += 1 while the ring fills, else local_ptr = (local_ptr + 1) % window.
+ * One single-thread launch; requires pool->ring_state.
+ */
+WGKV_API int wgkv_ring_advance(const wgkv_pool* pool, void* stream);
 
 /* ---- (a5, a6) decode: ring append + attention lengths --------------------- */
 /*
  * Writes k_new/v_new (B, Hk, D; strides sb, sh) into ring slot `insert_pos` of `layer`, pre_k_new into
  * local_pre_key when non-NULL, and cache_seqlens[b, h] = cur_local_len + global_lengths[layer, b, h]
  * (modeling_layers.py:1390-1400, :1429-1432).  The admission bit of the new token is written by
- * wgkv_gate_scores straight into local_is_global.
+ * wgkv_gate_scores straight into local_is_global.  insert_pos = WGKV_RING_ON_DEVICE (pool->ring_state
+ * set): insert_pos and cur_local_len are taken from ring_state (cur_local_len is then ignored).
  */
 WGKV_API int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
                                 const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
@@ -159,6 +181,7 @@ WGKV_API int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos
  * self_attn_forward_patch :1579 + decode_wrapper :1390-1400, :1429-1432).  Gate inputs are the
  * (B, Hk, D) rows pre_k_new / k_new / v_new selected by input_mask (bit 0 pre_k, 1 post_k = k_new,
  * 2 v = v_new).  Run the layer-0 promotion (wgkv_promote) before this, as it reads the old bit.
+ * insert_pos = WGKV_RING_ON_DEVICE reads the position from ring_state, as wgkv_decode_append does.
  */
 WGKV_API int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
                                      const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh, const uint16_t* k_new,
@@ -166,6 +189,41 @@ WGKV_API int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int inser
                                      int input_mask, const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
                                      const uint16_t* b2, const uint16_t* norm_w, float rms_eps, int inner, int act,
                                      float threshold, int32_t* cache_seqlens, void* stream);
+
+/*
+ * Decode prologue fused into the above (the q/k/v projection epilogue of the patched attention
+ * layers, modeling_llama.py:265-271 and modeling_qwen3.py:236-239, followed by the gate and the
+ * ring append).  qkv is each sequence's projection row [q heads | k heads | v heads] x D bf16, rows
+ * qkv_sb elements apart.  For every (b, kv head h): optional RMS norm of the k row and the q rows
+ * with k_norm / q_norm (D bf16 weights, eps qk_eps; Qwen3), then RoPE at position *position with
+ * rope_cos / rope_sin tables (n_positions, D) bf16, rounding as the bf16 torch expressions
+ * x*cos + rotate_half(x)*sin do.  The rotated q rows of h's query heads go to q_out (B, q_heads, D);
+ * the k row before RoPE is the gate's pre_k, the rotated k row its post_k and the ring's key.  With
+ * w1 == NULL (deferred gating) no gate runs and pre_k goes into local_pre_key.  A position outside
+ * [0, n_positions) is clamped and flags WGKV_ERR_BAD_POSITION.
+ */
+WGKV_API int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                  const uint16_t* qkv, int64_t qkv_sb, int q_heads, const uint16_t* q_norm,
+                                  const uint16_t* k_norm, float qk_eps, const uint16_t* rope_cos,
+                                  const uint16_t* rope_sin, const int64_t* position, int64_t n_positions,
+                                  uint16_t* q_out, int input_mask, const uint16_t* w1, const uint16_t* b1,
+                                  const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
+                                  int inner, int act, float threshold, int32_t* cache_seqlens, void* stream);
+
+/* ---- decoder plumbing of the end-to-end driver (no reference counterpart on the hot path) ---- */
+/*
+ * out[r] = (x[r] * rsqrt(mean(x[r]^2) + eps)).to(bf16) * weight, rows of `cols` bf16 (cols % 8 == 0,
+ * cols <= 8192), row strides in elements (multiples of 8), 16-byte aligned pointers.  The RMSNorm
+ * of the Llama / Qwen3 decoder layers around the patched attention (modeling_llama.py decoder layer).
+ */
+WGKV_API int wgkv_rms_norm(const uint16_t* x, int64_t x_stride, const uint16_t* weight, int rows, int cols,
+                           float eps, uint16_t* out, int64_t out_stride, void* stream);
+/*
+ * out[r, j] = silu(gate_up[r, j]).to(bf16) * gate_up[r, inter + j]: the MLP activation of the same
+ * decoder layers on a fused [gate | up] projection (inter % 8 == 0).
+ */
+WGKV_API int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows, int inter, uint16_t* out,
+                           int64_t out_stride, void* stream);
 
 /* ---- (a9-a11) vertical-slash sparse indices -------------------------------- */
 /*

@@ -316,6 +316,19 @@ __global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs 
 // ============================================================================
 // decode: ring append + cache_seqlens
 // ============================================================================
+// ins < 0: the position lives in pool.ring_state = {local_length, local_ptr} (decode_wrapper :1390-1396)
+__device__ __forceinline__ void ring_position(const wgkv_pool& P, int& ins, int& cur) {
+  if (ins >= 0) return;
+  const int len = P.ring_state[0];
+  if (len < P.window) {
+    ins = len;
+    cur = len + 1;
+  } else {
+    ins = P.ring_state[1];
+    cur = P.window;
+  }
+}
+
 __global__ void __launch_bounds__(256) decode_append_kernel(PoolArgs pa, int layer, int ins, int cur, RowSrc K,
                                                             RowSrc V, RowSrc PK, int32_t* cache_seqlens) {
   const wgkv_pool& P = pa.P;
@@ -323,6 +336,7 @@ __global__ void __launch_bounds__(256) decode_append_kernel(PoolArgs pa, int lay
   const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (i >= BH) return;
+  ring_position(P, ins, cur);
   const int b = i / Hk, h = i - b * Hk;
   const int64_t row = (int64_t(layer) * BH + i) * P.window + ins;
   copy_row<false>(P.k + row * D, K.p + b * K.sb + h * K.sh, D, lane, 32);
@@ -341,6 +355,10 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
   const wgkv_pool& P = pa.P;
   const int N = P.layers * P.batch * P.kv_heads;
   const int W = P.window, T = P.page, D = P.head_dim;
+  if (ptr < 0) {  // position on the device: promote only once the ring is full (:1470)
+    if (P.ring_state[0] < W) return;
+    ptr = P.ring_state[1];
+  }
   const int per = (N + kPromoteThreads - 1) / kPromoteThreads;
   const int i0 = threadIdx.x * per;  // contiguous entries keep the (layer, b, h) allocation order
   __shared__ int wsum[kPromoteThreads / 32];
@@ -418,6 +436,12 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
   }
 }
 
+// local_length / local_ptr update after the last layer of a decode step (:1408-1413)
+__global__ void ring_advance_kernel(int32_t* rs, int W) {
+  if (rs[0] < W) rs[0] += 1;
+  else rs[1] = rs[1] + 1 == W ? 0 : rs[1] + 1;
+}
+
 // ============================================================================
 // decode: gate on the new key + ring append + cache_seqlens, one CTA per (b, h)
 // ============================================================================
@@ -431,20 +455,92 @@ struct DecodeGateParams {
   float eps, thr;
 };
 
-__global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArgs pa, DecodeGateParams g, int layer,
-                                                                          int ins, int cur, RowSrc K, RowSrc V,
-                                                                          int32_t* cache_seqlens) {
+// Optional decode prologue fused in front of the gate (modeling_llama.py:265-271, modeling_qwen3.py:
+// 236-239): the q/k/v projection row of each sequence, [q heads | k heads | v heads] x D, gets the
+// optional per-head RMS norm (q_norm / k_norm), then RoPE at the device-side position; the k row
+// before RoPE is the gate's pre_k.  Element-wise roundings follow the bf16 torch expressions
+// x * cos + rotate_half(x) * sin and (x * rsqrt(mean(x^2) + eps)).to(bf16) * w.
+struct RopeParams {
+  const uint16_t* qkv;  // NULL: no prologue (inputs come from DecodeGateParams / K / V)
+  int64_t sb;           // elements between sequences
+  int Hq;
+  const uint16_t *q_norm, *k_norm;
+  float eps;
+  const uint16_t *cos, *sin;  // (n_pos, D) bf16
+  const int64_t* pos;
+  int64_t n_pos;
+  uint16_t* q_out;  // (B, Hq, D) contiguous
+  int sel[3];       // gate input -> staged row (0 pre_k, 1 rotated k, 2 v)
+};
+
+// RMS-norm (optional) + RoPE of one D-row by the whole block (thread t owns element t).
+WGKV_DEV void norm_rope_row(const uint16_t* src, const uint16_t* norm, float eps, float c, float s, int D,
+                            float* xbuf, float* red, uint16_t* pre_out, uint16_t* rot_out) {
+  const int tid = threadIdx.x;
+  float x = tid < D ? bf2f(src[tid]) : 0.f;
+  if (norm) {
+    float ss = x * x;
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < kDgaThreads / 32; ++w) tot += red[w];
+    const float inv = rsqrtf(tot / float(D) + eps);
+    if (tid < D) x = bf16_round(bf16_round(x * inv) * bf2f(norm[tid]));
+  }
+  if (tid < D) {
+    xbuf[tid] = x;
+    if (pre_out) pre_out[tid] = f2bf(x);
+  }
+  __syncthreads();
+  if (tid < D) {
+    const int hd = D / 2;
+    const float xr = tid < hd ? -xbuf[tid + hd] : xbuf[tid - hd];
+    rot_out[tid] = f2bf(bf16_round(x * c) + bf16_round(xr * s));
+  }
+  __syncthreads();  // xbuf / red are reused by the next row
+}
+
+__global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArgs pa, DecodeGateParams g, RopeParams R,
+                                                                          int layer, int ins, int cur, RowSrc K,
+                                                                          RowSrc V, int32_t* cache_seqlens) {
   const wgkv_pool& P = pa.P;
   const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
   const int i = blockIdx.x, b = i / Hk, h = i - b * Hk;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  ring_position(P, ins, cur);
   // the paged-decode launch that follows may start its set-up now (it waits for this grid's results)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float xs[384];
   __shared__ float part[kDgaThreads / 32];
+  __shared__ __align__(16) uint16_t stage[3][128];
+  const int64_t row = (int64_t(layer) * BH + i) * P.window + ins;
+  const uint16_t* k_src = K.p + b * K.sb + h * K.sh;
+  const uint16_t* v_src = V.p + b * V.sb + h * V.sh;
+  if (R.qkv) {
+    int64_t pos = *R.pos;
+    if (pos < 0 || pos >= R.n_pos) {
+      if (tid == 0) set_error(P.err, WGKV_ERR_BAD_POSITION);
+      pos = pos < 0 ? 0 : R.n_pos - 1;
+    }
+    const float c = tid < D ? bf2f(R.cos[pos * D + tid]) : 0.f;
+    const float sn = tid < D ? bf2f(R.sin[pos * D + tid]) : 0.f;
+    const uint16_t* qkv = R.qkv + b * R.sb;
+    const int G = R.Hq / Hk;
+    if (tid < D) stage[2][tid] = qkv[int64_t(R.Hq + Hk + h) * D + tid];
+    norm_rope_row(qkv + int64_t(R.Hq + h) * D, R.k_norm, R.eps, c, sn, D, xs, part, stage[0], stage[1]);
+    for (int q = 0; q < G; ++q) {
+      const int hq = h * G + q;
+      norm_rope_row(qkv + int64_t(hq) * D, R.q_norm, R.eps, c, sn, D, xs, part, nullptr,
+                    R.q_out + (int64_t(b) * R.Hq + hq) * D);
+    }
+    k_src = stage[1];
+    v_src = stage[2];
+    if (!g.w1 && P.local_pre_key) copy_row<false>(P.local_pre_key + row * D, stage[0], D, tid, kDgaThreads);
+  }
   // ---- gate input row(s): one warp per input, optional RMS norm, rounded to bf16 ----
-  if (warp < g.n_in) {
-    const uint16_t* src = g.in[warp].p + b * g.in[warp].sb + h * g.in[warp].sh;
+  if (g.w1 && warp < g.n_in) {
+    const uint16_t* src = R.qkv ? stage[R.sel[warp]] : g.in[warp].p + b * g.in[warp].sb + h * g.in[warp].sh;
     const int per = D / 32;
     float x[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -465,10 +561,10 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
       if (j < per) xs[warp * D + lane * per + j] = x[j];
   }
   // ---- ring append (independent of the gate) ----
-  const int64_t row = (int64_t(layer) * BH + i) * P.window + ins;
-  copy_row<false>(P.k + row * D, K.p + b * K.sb + h * K.sh, D, tid, kDgaThreads);
-  copy_row<false>(P.v + row * D, V.p + b * V.sb + h * V.sh, D, tid, kDgaThreads);
+  copy_row<false>(P.k + row * D, k_src, D, tid, kDgaThreads);
+  copy_row<false>(P.v + row * D, v_src, D, tid, kDgaThreads);
   if (tid == 0 && cache_seqlens) cache_seqlens[i] = cur + P.global_lengths[layer * BH + i];
+  if (!g.w1) return;  // deferred gating: the ring is rescored as a whole later
   __syncthreads();
   // ---- hidden layer: a thread per neuron (W1 row read as 16-byte vectors), fp32 dot products ----
   const uint16_t* w1h = g.w1 + int64_t(h) * g.inner * g.I;
@@ -504,6 +600,11 @@ bool pool_ok(const wgkv_pool* P) {
   return P && P->k && P->v && P->block_table && P->global_lengths && P->local_is_global && P->next_free_block &&
          P->layers > 0 && P->batch > 0 && P->kv_heads > 0 && (P->head_dim == 64 || P->head_dim == 128) &&
          P->page > 0 && P->window > 0 && P->window % P->page == 0 && P->total_blocks > 0;
+}
+
+// a host ring position, or WGKV_RING_ON_DEVICE with the pool's device copy present
+bool ring_pos_ok(const wgkv_pool* P, int pos) {
+  return pos == WGKV_RING_ON_DEVICE ? P->ring_state != nullptr : (pos >= 0 && pos < P->window);
 }
 
 }  // namespace
@@ -627,10 +728,16 @@ extern "C" int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len,
 }
 
 extern "C" int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream) {
-  if (!pool_ok(pool) || local_ptr < 0 || local_ptr >= pool->window) return WGKV_EINVAL;
+  if (!pool_ok(pool) || !ring_pos_ok(pool, local_ptr)) return WGKV_EINVAL;
   PoolArgs pa{*pool};
   if (pool->layers * pool->batch * pool->kv_heads > kPromoteThreads * kPromoteMaxPer) return WGKV_EINVAL;
   promote_kernel<<<1, kPromoteThreads, 0, as_stream(stream)>>>(pa, local_ptr);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_ring_advance(const wgkv_pool* pool, void* stream) {
+  if (!pool_ok(pool) || !pool->ring_state) return WGKV_EINVAL;
+  ring_advance_kernel<<<1, 1, 0, as_stream(stream)>>>(pool->ring_state, pool->window);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -638,8 +745,7 @@ extern "C" int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_p
                                   const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
                                   int64_t v_sb, int64_t v_sh, const uint16_t* pre_k_new, int64_t pk_sb, int64_t pk_sh,
                                   int32_t* cache_seqlens, void* stream) {
-  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || insert_pos < 0 || insert_pos >= pool->window || !k_new ||
-      !v_new)
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || !ring_pos_ok(pool, insert_pos) || !k_new || !v_new)
     return WGKV_EINVAL;
   if (((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
         reinterpret_cast<uintptr_t>(pre_k_new)) & 3) || ((k_sb | k_sh | v_sb | v_sh | pk_sb | pk_sh) & 1))
@@ -659,7 +765,7 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
                                        const uint16_t* b1, const uint16_t* w2, const uint16_t* b2,
                                        const uint16_t* norm_w, float rms_eps, int inner, int act, float threshold,
                                        int32_t* cache_seqlens, void* stream) {
-  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || insert_pos < 0 || insert_pos >= pool->window ||
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || !ring_pos_ok(pool, insert_pos) ||
       !k_new || !v_new || !w1 || !b1 || !w2 || !b2 || inner <= 0 || (act != 0 && act != 1))
     return WGKV_EINVAL;
   if (((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
@@ -689,7 +795,58 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
   PoolArgs pa{*pool};
   RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0};
   const int BH = pool->batch * pool->kv_heads;
-  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, layer, insert_pos, cur_local_len, K, V,
-                                                                       cache_seqlens);
+  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, RopeParams{}, layer, insert_pos,
+                                                                       cur_local_len, K, V, cache_seqlens);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
+                                    const uint16_t* qkv, int64_t qkv_sb, int q_heads, const uint16_t* q_norm,
+                                    const uint16_t* k_norm, float qk_eps, const uint16_t* rope_cos,
+                                    const uint16_t* rope_sin, const int64_t* position, int64_t n_positions,
+                                    uint16_t* q_out, int input_mask, const uint16_t* w1, const uint16_t* b1,
+                                    const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
+                                    int inner, int act, float threshold, int32_t* cache_seqlens, void* stream) {
+  if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || !ring_pos_ok(pool, insert_pos) || !qkv || !rope_cos ||
+      !rope_sin || !position || n_positions <= 0 || !q_out || q_heads <= 0 || q_heads % pool->kv_heads)
+    return WGKV_EINVAL;
+  const int D = pool->head_dim;
+  if (qkv_sb < int64_t(q_heads + 2 * pool->kv_heads) * D) return WGKV_EINVAL;
+  DecodeGateParams g = {};
+  RopeParams R = {};
+  R.qkv = qkv;
+  R.sb = qkv_sb;
+  R.Hq = q_heads;
+  R.q_norm = q_norm;
+  R.k_norm = k_norm;
+  R.eps = qk_eps;
+  R.cos = rope_cos;
+  R.sin = rope_sin;
+  R.pos = position;
+  R.n_pos = n_positions;
+  R.q_out = q_out;
+  if (w1) {
+    if (!b1 || !w2 || !b2 || inner <= 0 || (act != 0 && act != 1) || (reinterpret_cast<uintptr_t>(w1) & 15))
+      return WGKV_EINVAL;
+    int n = 0;
+    for (int s = 0; s < 3; ++s) {
+      if (!(input_mask & (1 << s))) continue;
+      R.sel[n] = s;
+      g.norm[n] = norm_w ? norm_w + s * D : nullptr;
+      ++n;
+    }
+    if (n == 0 || n * D > 384 || (n * D) % 8) return WGKV_EINVAL;
+    g.n_in = n;
+    g.I = n * D;
+    g.inner = inner;
+    g.act = act;
+    g.w1 = w1; g.b1 = b1; g.w2 = w2; g.b2 = b2;
+    g.eps = rms_eps;
+    g.thr = threshold;
+  }
+  PoolArgs pa{*pool};
+  const int BH = pool->batch * pool->kv_heads;
+  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, R, layer, insert_pos, cur_local_len,
+                                                                       RowSrc{}, RowSrc{}, cache_seqlens);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

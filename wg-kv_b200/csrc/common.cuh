@@ -119,6 +119,9 @@ WGKV_DEV uint32_t pack_bf16x2(float lo, float hi) {
 
 WGKV_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// bf16 bit pattern of x (round to nearest even)
+WGKV_DEV uint16_t f2bf(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a tile
 // written by TMA with CU_TENSOR_MAP_SWIZZLE_128B (128-byte rows, tile base
 // 1024-byte aligned): the chunk index is XORed with row % 8.

@@ -12,6 +12,7 @@ from .decode import (  # noqa: F401
     paged_decode,
 )
 from .gate import GatingPredictor, GatingRMSNorm, load_gate_checkpoint  # noqa: F401
+from .graph import DecodeGraph  # noqa: F401
 from .indices import generate_sparse_indices, sparse_indices_into  # noqa: F401
 from .layers import (  # noqa: F401
     decode_wrapper,
@@ -19,9 +20,10 @@ from .layers import (  # noqa: F401
     prefill_wrapper,
     refresh_local_is_global,
     self_attn_forward_patch,
+    self_attn_decode_fused,
     self_attn_forward_patch_inference,
 )
-from .pool import WgkvPool, init_pool  # noqa: F401
+from .pool import RING_ON_DEVICE, WgkvPool, advance_host_ring, init_pool, ring_to_device  # noqa: F401
 from .prefill import sparse_attn_func, sparse_attn_func_pooled, sparse_attn_func_wrapper  # noqa: F401
 from .runtime import check_errors  # noqa: F401
 
@@ -34,6 +36,7 @@ def attach(attn, config=None):
     if config is not None:
         attn.config = config
     attn.self_attn_forward_patch = self_attn_forward_patch
+    attn.self_attn_decode_fused = self_attn_decode_fused
     attn.prefill_wrapper = prefill_wrapper
     attn.decode_wrapper = decode_wrapper
     attn.prefill_kernel = sparse_attn_func_wrapper

@@ -90,14 +90,16 @@ class _Lib:
 # kernels each compute entry point launches (for the benchmark's launch count)
 KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_append": 1, "wgkv_decode_gate_append": 1, "wgkv_promote": 1,
                     "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1, "wgkv_sparse_prefill_pooled": 1, "wgkv_gather_columns": 1,
-                    "wgkv_paged_decode_noalloc": 1}
+                    "wgkv_paged_decode_noalloc": 1, "wgkv_ring_advance": 1, "wgkv_decode_prologue": 1,
+                    "wgkv_rms_norm": 1, "wgkv_silu_mul": 1}
 
 
 lib = _Lib()
 
 STATUS = {0: "ok", -1: "invalid argument", -2: "CUDA error", -3: "workspace too small"}
 ERR_BITS = {0x1: "tokens exceed max_tokens_per_head", 0x2: "pool exhausted (allocation exceeds total_blocks)",
-            0x4: "a device wait timed out", 0x8: "page id out of range"}
+            0x4: "a device wait timed out", 0x8: "page id out of range",
+            0x10: "RoPE position outside the tables"}
 
 
 def check(status: int, what: str):

@@ -148,6 +148,29 @@ class GatingPredictor(nn.Module):
         check(st, "wgkv_decode_gate_append")
 
 
+    def decode_prologue(self, cache, layer, insert_pos, cur_local_len, qkv, q_heads, position, rope_cos, rope_sin,
+                        q_out, threshold, q_norm=None, k_norm=None, qk_eps=1e-6, gate=True):
+        """``wgkv_decode_prologue``: q/k norm + RoPE of the raw projection rows ``qkv`` (B, (Hq + 2 Hk) D),
+        then the fused gate + ring append of :meth:`decode_admit_append` (``gate=False``: deferred
+        gating, pre_k into the ring's pre-key store).  Rotated queries go to ``q_out`` (B, Hq, D)."""
+        assert qkv.dim() == 2 and qkv.stride(1) == 1 and qkv.dtype == torch.bfloat16
+        assert q_out.is_contiguous() and rope_cos.is_contiguous() and rope_sin.is_contiguous()
+        if gate:
+            w1, b1, w2, b2 = (_bf16(x) for x in (self.conv1.weight, self.conv1.bias, self.conv2.weight,
+                                                  self.conv2.bias))
+            nw = self._norm_weights(qkv.device)
+            gp = (self.input_mask, w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
+                  nw.data_ptr() if nw is not None else None, self._eps(), self.inner_dim, self.act)
+        else:
+            gp = (0, None, None, None, None, None, 0.0, 0, 0)
+        st = lib.wgkv_decode_prologue(pool_ref(cache), layer, insert_pos, cur_local_len, qkv.data_ptr(),
+                                      qkv.stride(0), q_heads, q_norm.data_ptr() if q_norm is not None else None,
+                                      k_norm.data_ptr() if k_norm is not None else None, float(qk_eps),
+                                      rope_cos.data_ptr(), rope_sin.data_ptr(), position.data_ptr(),
+                                      rope_cos.shape[0], q_out.data_ptr(), *gp, float(threshold),
+                                      cache.cache_seqlens.data_ptr(), stream_ptr(qkv.device))
+        check(st, "wgkv_decode_prologue")
+
 def load_gate_checkpoint(modules, state, prefix="model.layers.{i}.self_attn.g_predictors.", strict=True):
     """Load a WG-KV gate checkpoint into per-layer gates.
 

@@ -24,7 +24,7 @@ import torch
 
 from ._lib import check, lib
 from .indices import sparse_indices_into
-from .pool import init_pool, pool_ref
+from .pool import RING_ON_DEVICE, init_pool, pool_ref
 from .prefill import sparse_attn_func, sparse_attn_func_pooled, sparse_attn_func_wrapper
 from .runtime import stream_ptr, workspace
 
@@ -43,6 +43,15 @@ def _maybe_init(self, past_key_value, batch_size, key_states):
                   device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)))
     elif self.layer_idx == 0:
         raise AssertionError("prefill on an initialised cache (the reference asserts the same, :1197)")
+
+
+def _device_ring(cache):
+    """True while decode steps take the ring position from ``cache.ring_state`` (graph capture)."""
+    return getattr(cache, "wgkv_device_ring", False)
+
+
+def _promote_now(cache, W):
+    return _device_ring(cache) or cache.local_length == W
 
 
 def _s4(t):
@@ -82,8 +91,12 @@ def prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, val
 
 
 def migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head):
-    """Lazy promotion of every (layer, b, h) ring slot at local_ptr (:674-763), one launch."""
-    st = lib.wgkv_promote(pool_ref(past_key_value), int(past_key_value.local_ptr), stream_ptr(device))
+    """Lazy promotion of every (layer, b, h) ring slot at local_ptr (:674-763), one launch.
+
+    With the device ring (``wgkv_device_ring``) the slot, and whether the ring is full yet, are
+    read on the device, so the launch is made on every step."""
+    ptr = RING_ON_DEVICE if _device_ring(past_key_value) else int(past_key_value.local_ptr)
+    st = lib.wgkv_promote(pool_ref(past_key_value), ptr, stream_ptr(device))
     check(st, "wgkv_promote")
 
 
@@ -115,13 +128,19 @@ def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, valu
         insert_pos = past_key_value.local_ptr
         cur = W
     defer = past_key_value.local_pre_key is not None
+    dr = _device_ring(past_key_value)
     if not appended:
-        _append(self, past_key_value, l, insert_pos, cur, pre_key, key_states, value_states, defer, device)
+        _append(self, past_key_value, l, RING_ON_DEVICE if dr else insert_pos, cur, pre_key, key_states,
+                value_states, defer, device)
     if g_mask is not None:
+        if dr:
+            raise NotImplementedError("a precomputed g_mask needs the host ring position (no device ring)")
         past_key_value.local_is_global[l, :, :, insert_pos] = g_mask[:, :, 0].to(torch.uint8)
     elif defer and insert_pos == W - 1:
         refresh_local_is_global(self, past_key_value, device)
     if l == c.num_hidden_layers - 1:
+        if dr:
+            check(lib.wgkv_ring_advance(pool_ref(past_key_value), stream_ptr(device)), "wgkv_ring_advance")
         if past_key_value.local_length < W:
             past_key_value.local_length = cur
         else:
@@ -161,7 +180,7 @@ def self_attn_forward_patch_inference(self, past_key_value, input_shape, query_s
         g_mask = (g_scores > c.g_threshold).to(torch.uint8)
     assert c.local_window_size % c.block_size == 0
     local_blocks_per_head = c.local_window_size // c.block_size
-    if (not is_prefilling) and self.layer_idx == 0 and past_key_value.local_length == c.local_window_size:
+    if (not is_prefilling) and self.layer_idx == 0 and _promote_now(past_key_value, c.local_window_size):
         migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
     if is_prefilling:
         return self.prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states,
@@ -201,9 +220,11 @@ def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, i
     W = c.local_window_size
     local_blocks_per_head = W // c.block_size
     l = self.layer_idx
-    if l == 0 and past_key_value.local_length == W:
+    if l == 0 and _promote_now(past_key_value, W):
         migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
-    if past_key_value.local_length < W:
+    if _device_ring(past_key_value):
+        insert_pos, cur = RING_ON_DEVICE, 0
+    elif past_key_value.local_length < W:
         insert_pos, cur = past_key_value.local_length, past_key_value.local_length + 1
     else:
         insert_pos, cur = past_key_value.local_ptr, W
@@ -213,3 +234,36 @@ def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, i
     out = self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, None,
                               local_blocks_per_head, appended=True)
     return out, None, None
+
+
+def self_attn_decode_fused(self, past_key_value, qkv, q_heads, position, rope_cos, rope_sin, q_norm=None,
+                           k_norm=None, qk_eps=1e-6):
+    """Decode step of ``self_attn_forward_patch`` (gating_mode 3) fed by the raw q/k/v projection rows.
+
+    The patched layers rotate q/k and keep the pre-RoPE key before calling the patch
+    (src/modeling_llama.py:265-287, src/modeling_qwen3.py:236-239); here that prologue runs inside
+    the gate + append launch (``wgkv_decode_prologue``): optional q/k RMS norm, RoPE at the device
+    position ``position`` (1-element int64) from the (n, D) tables, gate on the pre-RoPE key (or,
+    with g_defer, the pre-key store), ring append, lengths.  Then the layer-0 promotion order,
+    the deferred rescoring and the paged attention are those of the unfused patch.
+    qkv (B, (Hq + 2 Hk) D) bf16 -> attention output (B, 1, Hq, D)."""
+    c = _cfg(self)
+    W = c.local_window_size
+    l = self.layer_idx
+    device = qkv.device
+    B = qkv.shape[0]
+    if l == 0 and _promote_now(past_key_value, W):
+        migrate_local_kv_to_global(self, past_key_value, device, W // c.block_size)
+    if _device_ring(past_key_value):
+        insert_pos, cur = RING_ON_DEVICE, 0
+    elif past_key_value.local_length < W:
+        insert_pos, cur = past_key_value.local_length, past_key_value.local_length + 1
+    else:
+        insert_pos, cur = past_key_value.local_ptr, W
+    q = torch.empty(B, q_heads, self.head_dim, dtype=qkv.dtype, device=device)
+    defer = bool(getattr(c, "g_defer", False))
+    self.g_predictors.decode_prologue(past_key_value, l, insert_pos, cur, qkv, q_heads, position, rope_cos,
+                                      rope_sin, q, c.g_threshold, q_norm=q_norm, k_norm=k_norm, qk_eps=qk_eps,
+                                      gate=not defer)
+    return self.decode_wrapper(self, past_key_value, q.view(B, q_heads, 1, self.head_dim), None, None, None,
+                               device, None, W // c.block_size, appended=True)

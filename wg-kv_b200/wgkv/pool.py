@@ -38,6 +38,7 @@ class WgkvPool(ctypes.Structure):
         ("page", ctypes.c_int32),
         ("max_blocks_per_head", ctypes.c_int32),
         ("max_tokens_per_head", ctypes.c_int32),
+        ("ring_state", ctypes.c_void_p),
     ]
 
 
@@ -71,6 +72,9 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     cache.total_blocks = total_blocks
     cache.wgkv_batch = batch
     cache.cache_seqlens = torch.zeros(batch, kv_heads, dtype=torch.int32, device=dev)
+    # device copy of (local_length, local_ptr), used when a decode step runs as a CUDA graph
+    cache.ring_state = torch.zeros(2, dtype=torch.int32, device=dev)
+    cache.wgkv_device_ring = False
     s = WgkvPool()
     s.k = cache.block_pool_k.data_ptr()
     s.v = cache.block_pool_v.data_ptr()
@@ -84,6 +88,7 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     s.layers, s.batch, s.kv_heads, s.head_dim = layers, batch, kv_heads, head_dim
     s.window, s.page = window, page
     s.max_blocks_per_head, s.max_tokens_per_head = max_blocks_per_head, max_tokens_per_head
+    s.ring_state = cache.ring_state.data_ptr()
     cache.wgkv_pool = s
     cache.gated_kv_initialized = True
     return cache
@@ -91,3 +96,19 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
 
 def pool_ref(cache) -> int:
     return ctypes.addressof(cache.wgkv_pool)
+
+
+RING_ON_DEVICE = -1  # WGKV_RING_ON_DEVICE
+
+
+def ring_to_device(cache):
+    """Copy the host ring position (local_length, local_ptr) into ``cache.ring_state``."""
+    cache.ring_state.copy_(torch.tensor([cache.local_length, cache.local_ptr], dtype=torch.int32))
+
+
+def advance_host_ring(cache, window):
+    """The host-side update decode_wrapper makes after the last layer (:1408-1413)."""
+    if cache.local_length < window:
+        cache.local_length += 1
+    else:
+        cache.local_ptr = (cache.local_ptr + 1) % window
