@@ -770,7 +770,9 @@ def model_arm(args, rank, world, local_rank):
     per_step_launches = (wgkv.lib.launches - l0) // n_eager
     dg = m.decode_graph(cache)  # one more real step, eager, then captured
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("wgkv_timed")
     graph_ms, _ = sync_ms(lambda: [dg.replay() for _ in range(K)])
+    torch.cuda.nvtx.range_pop()
     clocks = clk.stop() if clk else None
     wgkv.check_errors()
     glen = cache.global_lengths.double().mean().item()

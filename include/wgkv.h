@@ -224,6 +224,15 @@ WGKV_API int wgkv_rms_norm(const uint16_t* x, int64_t x_stride, const uint16_t* 
  */
 WGKV_API int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows, int inter, uint16_t* out,
                            int64_t out_stride, void* stream);
+/*
+ * y[i, j] = sum_k x[i, k] * w[j, k] (+ residual[i, j]) for the few rows of a decode step
+ * (1 <= m <= 8): x (m, k) bf16 rows x_stride apart, w (n, k) bf16 row-major (a torch Linear
+ * weight), fp32 accumulation, y bf16 (or fp32 when out_f32, then without residual) rows y_stride
+ * apart.  residual may alias y (in-place y += x w^T).  k % 8 == 0, 16-byte aligned x and w.
+ */
+WGKV_API int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
+                              int64_t y_stride, int out_f32, const uint16_t* residual, int64_t r_stride,
+                              void* stream);
 
 /* ---- (a9-a11) vertical-slash sparse indices -------------------------------- */
 /*

@@ -151,3 +151,21 @@ def test_silu_mul_matches_torch(rows, inter):
     got = silu_mul(gu)
     ref = F.silu(gu[:, :inter]) * gu[:, inter:]
     torch.testing.assert_close(got.float(), ref.float(), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 2048, 8192), (1, 3072, 2048), (2, 16384, 2048), (3, 1000, 72), (8, 517, 4096),
+                                   (5, 128256, 256), (7, 9, 8)])
+def test_skinny_gemm_matches_fp32(m, n, k):
+    from wgkv.model import skinny_linear
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda") * 0.05).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    tol = dict(atol=1e-2 * (k / 64) ** 0.5 * 0.05 + 1e-3, rtol=1e-2)
+    got32 = skinny_linear(x, w, out_f32=True)
+    torch.testing.assert_close(got32, ref, atol=1e-3 * (k ** 0.5) * 0.05 + 1e-4, rtol=1e-4)
+    got = skinny_linear(x, w)
+    torch.testing.assert_close(got.float(), ref, **tol)
+    r = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+    r0 = r.float().clone()
+    skinny_linear(x, w, residual=r)  # in place
+    torch.testing.assert_close(r.float(), r0 + ref, **tol)

@@ -37,7 +37,6 @@ struct GateParams {
   int64_t msb, msh, mst;
 };
 
-WGKV_DEV float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
 WGKV_DEV uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 
 WGKV_DEV float act_fn(float x, int act) {

@@ -119,6 +119,8 @@ WGKV_DEV uint32_t pack_bf16x2(float lo, float hi) {
 
 WGKV_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+WGKV_DEV float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
+
 // bf16 bit pattern of x (round to nearest even)
 WGKV_DEV uint16_t f2bf(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
 

@@ -1,9 +1,13 @@
-// Element-wise plumbing of the decoder around the WG-KV attention path (the end-to-end driver):
-// RMSNorm and SiLU(gate) * up, one launch each, with the bf16 roundings of the torch expressions
-//   (x.float() * rsqrt(mean(x^2) + eps)).to(bf16) * w          (LlamaRMSNorm / Qwen3RMSNorm)
-//   silu(gate).to(bf16) * up                                    (LlamaMLP / Qwen3MLP act_fn(gate) * up)
-// Both are HBM-bound streams over rows; 16-byte vector loads, one CTA per row.
+// Plumbing of the decoder around the WG-KV attention path (the end-to-end driver):
+// * RMSNorm and SiLU(gate) * up, one launch each, with the bf16 roundings of the torch expressions
+//     (x.float() * rsqrt(mean(x^2) + eps)).to(bf16) * w        (LlamaRMSNorm / Qwen3RMSNorm)
+//     silu(gate).to(bf16) * up                                  (LlamaMLP / Qwen3MLP act_fn(gate) * up)
+//   HBM-bound streams over rows; 16-byte vector loads, one CTA per row.
+// * Skinny GEMM y = x W^T (+ residual) for the decode step's few rows (m <= 8): a weight-streaming
+//   kernel (every weight byte read once, 16-byte loads, several in flight per lane) that the
+//   library GEMMs do not reach at m = 1 on these shapes.
 #include "common.cuh"
+#include "runtime.h"
 
 namespace wgkv {
 namespace {
@@ -86,6 +90,123 @@ __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const uint16_t* g
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// skinny GEMM: block = 8 warps over `rpb` weight rows; the 8 / rpb warps of a row split K.
+// Every lane issues all the 16-byte weight loads of one pass (kSgUnroll, predicated) before using
+// them, so short rows cost one memory round trip.
+constexpr int kSgWarps = 8;
+constexpr int kSgUnroll = 8;
+
+template <int M>
+__global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16_t* __restrict__ x, int64_t xs,
+                                                                    const uint16_t* __restrict__ w, int n, int k,
+                                                                    int rpb, void* y, int64_t ys, int out_f32,
+                                                                    const uint16_t* res, int64_t rs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = kSgWarps / rpb;          // warps per row
+  const int row_in = warp % rpb, slice = warp / rpb;
+  const int row = blockIdx.x * rpb + row_in;
+  const int kc = k / 8;                   // 16-byte chunks per row
+  const int per = (kc + ks - 1) / ks;     // chunks per slice
+  const int c0 = slice * per, c1 = min(kc, c0 + per);
+  float acc[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.f;
+  if (row < n) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(row) * k);
+    for (int cb = c0 + lane; cb < c1; cb += 32 * kSgUnroll) {
+      uint4 wv[kSgUnroll];
+#pragma unroll
+      for (int u = 0; u < kSgUnroll; ++u)
+        wv[u] = cb + 32 * u < c1 ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);  // streamed once
+#pragma unroll
+      for (int u = 0; u < kSgUnroll; ++u) {
+        const int c = cb + 32 * u;
+        if (c >= c1) break;
+        float wf[8];
+        unpack8(wv[u], wf);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          float xf[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), xf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], wf[e], acc[m]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+    for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffff, acc[m], o);
+  __shared__ float part[kSgWarps][M];
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) part[warp][m] = acc[m];
+  }
+  __syncthreads();
+  // one thread per (row, m) sums the K slices of its row
+  const int t = threadIdx.x;
+  if (t < rpb * M) {
+    const int ri = t % rpb, m = t / rpb;
+    const int r = blockIdx.x * rpb + ri;
+    if (r < n) {
+      float v = 0.f;
+      for (int s2 = 0; s2 < ks; ++s2) v += part[s2 * rpb + ri][m];
+      if (res) v += bf2f(res[m * rs + r]);
+      if (out_f32) reinterpret_cast<float*>(y)[m * ys + r] = v;
+      else reinterpret_cast<uint16_t*>(y)[m * ys + r] = f2bf(v);
+    }
+  }
+}
+
+// Many rows (n >= 8 * 4 * SMs): persistent warps, one row at a time, grid-stride over rows; no
+// block barrier.
+template <int M>
+__global__ void __launch_bounds__(kSgWarps * 32) skinny_rows_kernel(const uint16_t* __restrict__ x, int64_t xs,
+                                                                    const uint16_t* __restrict__ w, int n, int k,
+                                                                    void* y, int64_t ys, int out_f32,
+                                                                    const uint16_t* res, int64_t rs) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kSgWarps + (threadIdx.x >> 5), nw = gridDim.x * kSgWarps;
+  const int kc = k / 8;
+  for (int row = gw; row < n; row += nw) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(row) * k);
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0.f;
+    for (int cb = lane; cb < kc; cb += 32 * kSgUnroll) {
+      uint4 wv[kSgUnroll];
+#pragma unroll
+      for (int u = 0; u < kSgUnroll; ++u)
+        wv[u] = cb + 32 * u < kc ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kSgUnroll; ++u) {
+        const int c = cb + 32 * u;
+        if (c >= kc) break;
+        float wf[8];
+        unpack8(wv[u], wf);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          float xf[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), xf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], wf[e], acc[m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float v = acc[m];
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+      if (lane == m) {
+        if (res) v += bf2f(res[m * rs + row]);
+        if (out_f32) reinterpret_cast<float*>(y)[m * ys + row] = v;
+        else reinterpret_cast<uint16_t*>(y)[m * ys + row] = f2bf(v);
+      }
+    }
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -113,5 +234,40 @@ extern "C" int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int row
   dim3 grid((inter / 8 + kRowThreads - 1) / kRowThreads, rows < 65535 ? rows : 65535);
   silu_mul_kernel<<<grid, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(gate_up, gu_stride, rows, inter, out,
                                                                                 out_stride);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
+                                int64_t y_stride, int out_f32, const uint16_t* residual, int64_t r_stride,
+                                void* stream) {
+  if (!x || !w || !y || m <= 0 || m > 8 || n <= 0 || k <= 0 || k % 8 || x_stride % 8 || !aligned16(x) ||
+      !aligned16(w) || (residual && out_f32))
+    return WGKV_EINVAL;
+  const int sms = device_sms();
+  if (sms <= 0) return WGKV_ECUDA;
+  // rows per block: as many as keep >= 4 blocks per SM; the block's other warps split K
+  int rpb = 1;
+  while (rpb < kSgWarps && int64_t(n) / (rpb * 2) >= 4 * sms) rpb *= 2;
+  const bool rows = rpb == kSgWarps && int64_t(n) >= int64_t(kSgWarps) * 8 * sms;
+  const int blocks = rows ? 8 * sms : (n + rpb - 1) / rpb;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define WGKV_SG(MM)                                                                                            \
+  if (rows)                                                                                                    \
+    skinny_rows_kernel<MM><<<blocks, kSgWarps * 32, 0, s>>>(x, x_stride, w, n, k, y, y_stride, out_f32,        \
+                                                            residual, r_stride);                              \
+  else                                                                                                         \
+    skinny_gemm_kernel<MM><<<blocks, kSgWarps * 32, 0, s>>>(x, x_stride, w, n, k, rpb, y, y_stride, out_f32,   \
+                                                            residual, r_stride)
+  switch (m) {
+    case 1: WGKV_SG(1); break;
+    case 2: WGKV_SG(2); break;
+    case 3: WGKV_SG(3); break;
+    case 4: WGKV_SG(4); break;
+    case 5: WGKV_SG(5); break;
+    case 6: WGKV_SG(6); break;
+    case 7: WGKV_SG(7); break;
+    default: WGKV_SG(8); break;
+  }
+#undef WGKV_SG
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

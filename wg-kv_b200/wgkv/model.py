@@ -79,6 +79,24 @@ def silu_mul(gu):
     return out
 
 
+def skinny_linear(x, w, residual=None, out_f32=False):
+    """``wgkv_skinny_gemm``: x (m <= 8, k) bf16 @ w (n, k)^T, fp32 accumulate; ``residual`` (m, n)
+    bf16 is added and receives the result in place; ``out_f32`` returns fp32 (no residual)."""
+    m, k = x.shape
+    n = w.shape[0]
+    assert x.stride(1) == 1 and w.is_contiguous() and m <= 8
+    if residual is not None:
+        y = residual
+        assert y.stride(1) == 1 and y.shape == (m, n)
+    else:
+        y = torch.empty(m, n, dtype=torch.float32 if out_f32 else x.dtype, device=x.device)
+    check(lib.wgkv_skinny_gemm(x.data_ptr(), x.stride(0), m, w.data_ptr(), n, k, y.data_ptr(), y.stride(0),
+                               int(out_f32), residual.data_ptr() if residual is not None else None,
+                               residual.stride(0) if residual is not None else 0, stream_ptr(x.device)),
+          "wgkv_skinny_gemm")
+    return y
+
+
 def _rotate_half(x):
     h = x.shape[-1] // 2
     return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
@@ -201,8 +219,14 @@ class WgkvDecoder:
     def _norm(self, x, w):
         return rms_norm(x, w, self.s.rms_eps) if self.fused else _rms(x, w, self.s.rms_eps)
 
+    def _skinny(self, rows):
+        return self.fused and rows <= 8
+
     def _qkv_rows(self, L, x_in):
-        return self._norm(x_in, L.in_norm) @ L.qkv.t()
+        x = self._norm(x_in, L.in_norm)
+        if self._skinny(x.numel() // x.shape[-1]):
+            return skinny_linear(x.reshape(-1, x.shape[-1]), L.qkv).view(*x.shape[:-1], -1)
+        return x @ L.qkv.t()
 
     def _qkv(self, L, x_in):
         s = self.s
@@ -232,12 +256,19 @@ class WgkvDecoder:
             h = h + (F.silu(gu[..., :I]) * gu[..., I:]) @ L.down.t()
             self._stop(t)
             return h
-        # residual adds as the GEMMs' beta = 1 epilogue; norm and activation one launch each
+        # residual adds fused into the projections; norm and activation one launch each
         h2 = h.view(-1, h.shape[-1])
-        h2.addmm_(a.reshape(h2.shape[0], -1), L.o.t())
-        t = self._time("mlp")
-        x = rms_norm(h2, L.post_norm, self.s.rms_eps)
-        h2.addmm_(silu_mul(x @ L.gate_up.t()), L.down.t())
+        a2 = a.reshape(h2.shape[0], -1)
+        if self._skinny(h2.shape[0]):
+            skinny_linear(a2, L.o, residual=h2)
+            t = self._time("mlp")
+            x = rms_norm(h2, L.post_norm, self.s.rms_eps)
+            skinny_linear(silu_mul(skinny_linear(x, L.gate_up)), L.down, residual=h2)
+        else:
+            h2.addmm_(a2, L.o.t())
+            t = self._time("mlp")
+            x = rms_norm(h2, L.post_norm, self.s.rms_eps)
+            h2.addmm_(silu_mul(x @ L.gate_up.t()), L.down.t())
         self._stop(t)
         return h
 
@@ -267,7 +298,10 @@ class WgkvDecoder:
             h = self._after_attn(L, h, o.reshape(B, T, -1))
         t = self._time("lm_head")
         x = self._norm(h[:, -1:].contiguous(), self.final_norm)
-        logits = (x @ self.lm_head.t()).float()[:, 0]
+        if self._skinny(B):
+            logits = skinny_linear(x.view(B, -1), self.lm_head, out_f32=True)
+        else:
+            logits = (x @ self.lm_head.t()).float()[:, 0]
         self._stop(t)
         return logits
 
