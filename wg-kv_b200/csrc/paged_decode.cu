@@ -62,7 +62,7 @@ template <int D, int S>
 size_t smem_bytes(int BH, int G) {
   size_t s = 1024;  // alignment slack
   s += size_t(Cfg<D, S>::kStages) * Cfg<D, S>::kStageBytes;
-  s += size_t(BH + 1 + kThreads) * 4;                   // prefix + scan scratch
+  s += size_t(BH + 1 + kThreads + 64) * 4;              // prefix + scan scratch
   s += size_t(kNCW) * G * (D + 2) * 4;                  // cross-warp merge
   s += 2 * Cfg<D, S>::kStages * 8 + 64;                 // barriers + flags
   return s;
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stage_base = smem;
   int* pre = reinterpret_cast<int*>(smem + C::kStages * C::kStageBytes);
   int* scan = pre + p.BH + 1;  // kThreads ints
-  float* merge = reinterpret_cast<float*>(scan + kThreads);
+  float* merge = reinterpret_cast<float*>(scan + kThreads + 64);
   const int G = p.G;
   uint64_t* full = reinterpret_cast<uint64_t*>(merge + kNCW * G * (D + 2) + 1);
   full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
@@ -111,19 +111,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i0 = min(BH, tid * per), i1 = min(BH, i0 + per);
     int sum = 0;
     for (int i = i0; i < i1; ++i) sum += (max(p.seqlens[i], 0) + 15) >> 4;
-    scan[tid] = sum;
+    // block-wide exclusive scan of the per-thread sums (warp shuffles, then the warp totals)
+    int x = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffff, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) scan[warp] = x;
     __syncthreads();
-    if (tid == 0) {
-      int run = 0;
-      for (int t = 0; t < kThreads; ++t) {
-        int v = scan[t];
-        scan[t] = run;
-        run += v;
+    if (warp == 0) {
+      int wt = lane < kThreads / 32 ? scan[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffff, wt, o);
+        if (lane >= o) wt += y;
       }
-      pre[BH] = run;
+      if (lane < kThreads / 32) scan[32 + lane] = wt;  // inclusive warp totals
+      if (lane == kThreads / 32 - 1) pre[BH] = wt;
     }
     __syncthreads();
-    int run = scan[tid];
+    scan[64 + tid] = (warp ? scan[32 + warp - 1] : 0) + x - sum;  // exclusive prefix of this thread
+    __syncthreads();
+    int run = scan[64 + tid];
     for (int i = i0; i < i1; ++i) {
       pre[i] = run;
       run += (max(p.seqlens[i], 0) + 15) >> 4;
@@ -388,21 +396,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kNCW));
       if (*flag) {
         __threadfence();
-        for (int e = ctid; e < G * D; e += 32 * kNCW) {
-          const int r = e / D;
-          float M = -INFINITY;
-          for (int c = c_first; c <= c_last; ++c)
-            M = fmaxf(M, __ldcg(p.part + size_t(bh + c) * G * (D + 2) + G * D + r));
-          float L = 0.f, A = 0.f;
-          if (M != -INFINITY) {
-            for (int c = c_first; c <= c_last; ++c) {
-              const float* sl = p.part + size_t(bh + c) * G * (D + 2);
-              const float f = exp2f(__ldcg(sl + G * D + r) - M);
-              L += __ldcg(sl + G * D + G + r) * f;
-              A += __ldcg(sl + e) * f;
-            }
+        const int np = c_last - c_first + 1;
+        const float* p0 = p.part + size_t(bh + c_first) * G * (D + 2);
+        // (m, l) of every partial, then its scale factor, staged in `merge`
+        float* mm = merge;             // [np][G]
+        float* ll = mm + np * G;       // [np][G]
+        float* rowL = ll + np * G;     // [G]
+        if (2 * np * G + G <= kNCW * G * (D + 2)) {
+          for (int t = ctid; t < np * G; t += 32 * kNCW) {
+            const float* sl = p0 + size_t(t / G) * G * (D + 2);
+            mm[t] = __ldcg(sl + G * D + t % G);
+            ll[t] = __ldcg(sl + G * D + G + t % G);
           }
-          p.out[size_t(bh) * G * D + e] = __bfloat16_as_ushort(__float2bfloat16_rn(L > 0.f ? A / L : 0.f));
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kNCW));
+          // row maxima and normalisers: one consumer warp per query head
+          for (int r = cw; r < G; r += kNCW) {
+            float M = -INFINITY;
+            for (int c = lane; c < np; c += 32) M = fmaxf(M, mm[c * G + r]);
+            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffff, M, o));
+            float L = 0.f;
+            for (int c = lane; c < np; c += 32) {
+              const float f = M == -INFINITY ? 0.f : exp2f(mm[c * G + r] - M);
+              mm[c * G + r] = f;  // scale factor of partial c, row r
+              L += ll[c * G + r] * f;
+            }
+            for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffff, L, o);
+            if (lane == 0) rowL[r] = L;
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kNCW));
+          for (int e = ctid; e < G * D; e += 32 * kNCW) {
+            const int r = e / D;
+            float A0 = 0.f, A1 = 0.f, A2 = 0.f, A3 = 0.f;
+            int c = 0;
+            for (; c + 4 <= np; c += 4) {  // four independent L2 loads in flight
+              const float v0 = __ldcg(p0 + size_t(c) * G * (D + 2) + e);
+              const float v1 = __ldcg(p0 + size_t(c + 1) * G * (D + 2) + e);
+              const float v2 = __ldcg(p0 + size_t(c + 2) * G * (D + 2) + e);
+              const float v3 = __ldcg(p0 + size_t(c + 3) * G * (D + 2) + e);
+              A0 = fmaf(v0, mm[c * G + r], A0);
+              A1 = fmaf(v1, mm[(c + 1) * G + r], A1);
+              A2 = fmaf(v2, mm[(c + 2) * G + r], A2);
+              A3 = fmaf(v3, mm[(c + 3) * G + r], A3);
+            }
+            for (; c < np; ++c) A0 = fmaf(__ldcg(p0 + size_t(c) * G * (D + 2) + e), mm[c * G + r], A0);
+            const float A = (A0 + A1) + (A2 + A3), L = rowL[r];
+            p.out[size_t(bh) * G * D + e] = __bfloat16_as_ushort(__float2bfloat16_rn(L > 0.f ? A / L : 0.f));
+          }
+        } else {
+          for (int e = ctid; e < G * D; e += 32 * kNCW) {
+            const int r = e / D;
+            float M = -INFINITY;
+            for (int c = c_first; c <= c_last; ++c)
+              M = fmaxf(M, __ldcg(p.part + size_t(bh + c) * G * (D + 2) + G * D + r));
+            float L = 0.f, A = 0.f;
+            if (M != -INFINITY) {
+              for (int c = c_first; c <= c_last; ++c) {
+                const float* sl = p.part + size_t(bh + c) * G * (D + 2);
+                const float f = exp2f(__ldcg(sl + G * D + r) - M);
+                L += __ldcg(sl + G * D + G + r) * f;
+                A += __ldcg(sl + e) * f;
+              }
+            }
+            p.out[size_t(bh) * G * D + e] = __bfloat16_as_ushort(__float2bfloat16_rn(L > 0.f ? A / L : 0.f));
+          }
         }
       }
     }
