@@ -721,7 +721,7 @@ def model_arm(args, rank, world, local_rank):
     shape = SHAPES[args.model]
     B, P, K, Wu = args.batch, args.prompt, args.steps, args.warmup
     n_eager = min(K, 32)
-    total = P + Wu + n_eager + 2 * K + 16
+    total = P + Wu + n_eager + 2 * K + 24
     m = WgkvDecoder(shape, batch=B, window=args.window, max_tokens_per_head=total + args.window + 64,
                     g_defer=not args.no_defer, max_positions=total, device=dev, seed=rank)
     m.calibrate_gates()
@@ -765,6 +765,8 @@ def model_arm(args, rank, world, local_rank):
     clk = ClockSampler(local_rank) if rank == 0 else None
     cache = SimpleNamespace()
     ttft, _ = sync_ms(lambda: m.prefill(ids, cache))
+    for _ in range(2):  # steady state: first-use costs (allocator segments, module loads) stay untimed
+        m.decode_step(cache)
     l0 = wgkv.lib.launches
     eager_ms, _ = sync_ms(lambda: [m.decode_step(cache) for _ in range(n_eager)])
     per_step_launches = (wgkv.lib.launches - l0) // n_eager
