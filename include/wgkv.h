@@ -25,6 +25,8 @@
  *   wgkv_sparse_indices       generate_sparse_indices :385-409 (+ generate_block_offset :321-349,
  *                             generate_column_index :352-381)
  *   wgkv_sparse_prefill       sparse_attn_func (vLLM fork) as called at :1366-1374
+ *   wgkv_quest_select         quest_select_blocks :452-576 (page bounds kept by prefill :1333-1347 and
+ *                             promotion :744-761)
  *   wgkv_paged_decode         flash_attn_with_kvcache_wrapper_triton_handle + split/reduce kernels :818-1140
  *                             (and the batched flash_attn_with_kvcache_wrapper :766-811)
  */
@@ -79,6 +81,9 @@ WGKV_API int wgkv_num_sms(void);
  *                    points accept WGKV_RING_ON_DEVICE in place of insert_pos / local_ptr and read the
  *                    position here, and wgkv_ring_advance moves it, so that one captured CUDA graph
  *                    replays every decode step.  NULL = positions come from the host only.
+ *   quest_min/max    optional (total_blocks, head_dim) bf16: element-wise min / max of the keys of every
+ *                    global page (quest_block_key_min / _max, :1232-1240), kept by wgkv_prefill_admit and
+ *                    wgkv_promote when set; read by wgkv_quest_select.  NULL = QUEST off.
  * The ring slot s of (layer l, batch b, head h) is pool row ((l*batch + b)*kv_heads + h)*window + s.
  */
 typedef struct wgkv_pool {
@@ -100,6 +105,8 @@ typedef struct wgkv_pool {
   int32_t max_blocks_per_head;
   int32_t max_tokens_per_head;
   int32_t* ring_state;
+  uint16_t* quest_min;
+  uint16_t* quest_max;
 } wgkv_pool;
 
 /* insert_pos / local_ptr value that means "read the position from pool->ring_state". */
@@ -209,6 +216,23 @@ WGKV_API int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_p
                                   uint16_t* q_out, int input_mask, const uint16_t* w1, const uint16_t* b1,
                                   const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
                                   int inner, int act, float threshold, int32_t* cache_seqlens, void* stream);
+
+/* ---- QUEST block selection (use_quest) ------------------------------------ */
+/*
+ * quest_select_blocks (:452-576) for every (b, h) of `layer`: score each full global page by
+ * max_g bf16(sum_d bf16(q_gd * (q_gd >= 0 ? quest_max : quest_min))), keep the ring pages
+ * (ceil(cur_local_len / page) of them), the best `capacity - 1` full pages (all when they fit; ties
+ * go to the lower position) and the trailing partial page, where capacity = min(ceil(max(budget -
+ * cur_local_len, 0) / page), global pages).  Writes out_seqlens (B, Hk) = the tokens kept and
+ * out_table (B, Hk, out_stride) = their page ids, ring pages first, then the global pages in
+ * position order -- inputs for wgkv_paged_decode.  q (B, q_heads, D) bf16, rows q_sb elements apart.
+ * cur_local_len = WGKV_RING_ON_DEVICE takes the ring length from pool->ring_state.  out_stride must
+ * be at least wgkv_quest_table_stride(window, page, token_budget, max_blocks_per_head).
+ */
+WGKV_API size_t wgkv_quest_table_stride(int window, int page, int token_budget, int max_blocks_per_head);
+WGKV_API int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local_len, const uint16_t* q, int64_t q_sb,
+                               int q_heads, int token_budget, int32_t* out_seqlens, int32_t* out_table,
+                               int64_t out_stride, void* stream);
 
 /* ---- decoder plumbing of the end-to-end driver (no reference counterpart on the hot path) ---- */
 /*

@@ -380,6 +380,7 @@ class PoolState:
     max_total_tokens: int
     max_tokens_per_head: int
     defer: bool = False
+    quest: bool = False
 
     def __post_init__(self):
         assert self.window % self.page == 0
@@ -398,6 +399,9 @@ class PoolState:
         self.local_ptr = 0
         self.local_length = 0
         self.next_free_block = Ly * B * Hk * self.local_pages
+        if self.quest:  # per-page key bounds (quest_block_key_min / _max, modeling_layers.py:1232-1240)
+            self.qmin = np.zeros((self.total_blocks, self.head_dim), np.float32)
+            self.qmax = np.zeros((self.total_blocks, self.head_dim), np.float32)
 
     def ring_row(self, l, b, h, slot):
         return ((l * self.batch + b) * self.kv_heads + h) * self.window + slot
@@ -437,6 +441,11 @@ class PoolState:
                 self.v[first * T:first * T + n] = v[b, h, idx]
                 self.global_lengths[l, b, h] = n
                 self.next_free_block += need
+                if self.quest:  # key bounds of every new page (:1333-1347)
+                    for pg in range(need):
+                        rows = self.k[(first + pg) * T:(first + pg) * T + min(T, n - pg * T)]
+                        self.qmin[first + pg] = rows.min(axis=0)
+                        self.qmax[first + pg] = rows.max(axis=0)
 
     # -- migrate_local_kv_to_global (modeling_layers.py:674-763) --------------
     def promote(self):
@@ -464,6 +473,10 @@ class PoolState:
         dst = phys * T + off
         self.k[dst] = self.k[src]
         self.v[dst] = self.v[src]
+        if self.quest:  # :744-761: a new page starts at the key, else min / max with it
+            kk = self.k[src]
+            self.qmin[phys] = np.where(need[:, None], kk, np.minimum(self.qmin[phys], kk))
+            self.qmax[phys] = np.where(need[:, None], kk, np.maximum(self.qmax[phys], kk))
         self.global_lengths[flat[:, 0], flat[:, 1], flat[:, 2]] = glen + 1
 
     # -- decode_wrapper state part (modeling_layers.py:1390-1413) -------------
@@ -504,6 +517,61 @@ class PoolState:
     def decode_tables(self, l, cur_local_len):
         """``cache_seqlens``/``block_table`` views of modeling_layers.py:1429-1436."""
         return (cur_local_len + self.global_lengths[l]).astype(np.int32), self.block_table[l]
+
+    def quest_scores(self, l, b, h, q):
+        """Block scores of quest_select_blocks (:495-504) for the head's full and partial global pages:
+        max over the G query heads of bf16(sum_d bf16(q_d * (q_d >= 0 ? kmax_d : kmin_d))).
+        q ``(G, D)`` (bf16 values); returns float32 scores (bf16 values), one per global page."""
+        T = self.page
+        glen = int(self.global_lengths[l, b, h])
+        nb = (glen + T - 1) // T
+        pages = self.block_table[l, b, h, self.local_pages:self.local_pages + nb].astype(np.int64)
+        sel = np.where(q[:, None, :] >= 0, self.qmax[pages][None], self.qmin[pages][None])  # (G, nb, D)
+        prod = bf16(q[:, None, :].astype(np.float32) * sel)
+        sc = bf16(prod.astype(np.float64).sum(-1).astype(np.float32))
+        return sc.max(axis=0) if nb else np.zeros(0, np.float32)
+
+    def quest_select(self, l, cur_local_len, q, token_budget):
+        """quest_select_blocks (modeling_layers.py:452-576) for every (b, h) of layer l.
+
+        q ``(B, Hq, D)``.  Returns (cache_seqlens ``(B, Hk)`` int32, list over (b, h) of the selected
+        page ids: ring pages, then the chosen full global pages in ascending position, then the
+        trailing partial page).  The reference lists the full pages in torch.topk order; the set is
+        what attention depends on.  Ties at the k-th score go to the lowest position (torch.topk
+        leaves their order unspecified)."""
+        T = self.page
+        B, Hk = self.batch, self.kv_heads
+        G = q.shape[1] // Hk
+        local_blocks = (cur_local_len + T - 1) // T
+        budget_blocks = (max(token_budget - cur_local_len, 0) + T - 1) // T
+        seqlens = np.zeros((B, Hk), np.int32)
+        tables = []
+        for b in range(B):
+            for h in range(Hk):
+                glen = int(self.global_lengths[l, b, h])
+                full, rem = divmod(glen, T)
+                nb = full + (rem > 0)
+                cap = min(budget_blocks, nb)
+                chosen = np.zeros(0, np.int64)
+                partial = False
+                if cap > 0:
+                    full_cap = cap - (1 if rem > 0 else 0)
+                    if full_cap > 0 and full > 0:
+                        if full_cap >= full:
+                            chosen = np.arange(full)
+                        else:
+                            sc = self.quest_scores(l, b, h, q[b, h * G:(h + 1) * G])[:full]
+                            order = np.lexsort((np.arange(full), -sc.astype(np.float64)))
+                            chosen = np.sort(order[:full_cap])
+                    if rem > 0:
+                        chosen = np.concatenate([chosen, [full]])
+                        partial = True
+                row = self.block_table[l, b, h]
+                pages = np.concatenate([row[:local_blocks], row[self.local_pages + chosen]]).astype(np.int32)
+                n_tok = len(chosen) * T + (rem - T if partial else 0)
+                seqlens[b, h] = cur_local_len + n_tok
+                tables.append(pages)
+        return seqlens, tables
 
     def paged_views(self):
         T, D = self.page, self.head_dim

@@ -133,24 +133,29 @@ def sdpa_rows_fp64(q, k, v, mask, rows, scale):
     return (p @ vv).transpose(1, 2)  # (B, rows, Hq, D)
 
 
-def make_self(m, cfg, layer_idx, gp, prefill_stub, decode_ref):
+def make_self(m, cfg, layer_idx, gp, prefill_stub, decode_ref, record=None):
     s = SimpleNamespace()
     s.layer_idx = layer_idx
     s.config = cfg
     s.head_dim = cfg.head_dim
+    s.num_key_value_groups = cfg.num_attention_heads // cfg.num_key_value_heads
     s.scaling = cfg.head_dim ** -0.5
     s.g_predictors = gp
     s.prefill_wrapper = m.prefill_wrapper
     s.decode_wrapper = m.decode_wrapper
     s.prefill_kernel = prefill_stub
-    s.decode_kernel_handle = lambda *a, **k: (lambda: decode_ref(*a, **k))
+    def handle(*a, **k):
+        if record is not None:  # (q, k_cache, v_cache, cache_seqlens, block_table, scale)
+            record["seqlens"], record["table"] = a[3].clone(), a[4].clone()
+        return lambda: decode_ref(*a, **k)
+    s.decode_kernel_handle = handle
     s.decode_kernel_executor = lambda f: f()
     return s
 
 
 def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, threshold,
                       n_decode, defer, seed, max_total_tokens, max_tokens_per_head, rows_out=16,
-                      inputs=("pre_k",), act="gelu"):
+                      inputs=("pre_k",), act="gelu", quest_budget=None):
     """Prefill of one sequence through every layer, then n_decode decode steps."""
     rng = np.random.default_rng(seed)
     G = Hq // Hk
@@ -176,7 +181,8 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
 
     cfg = SimpleNamespace(num_hidden_layers=Ly, num_key_value_heads=Hk, num_attention_heads=Hq, head_dim=D,
                           block_size=T, max_total_tokens=max_total_tokens, max_tokens_per_head=max_tokens_per_head,
-                          local_window_size=W, use_quest=False, g_defer=defer, snapkv_enabled=False,
+                          local_window_size=W, use_quest=quest_budget is not None,
+                          quest_token_budget=quest_budget, g_defer=defer, snapkv_enabled=False,
                           use_baseline=False, g_threshold=threshold, g_expand=inner / D, random_sparsity=None)
     pkv = SimpleNamespace()
     captured = {}
@@ -208,11 +214,14 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
         out["prefill_local_is_global"] = pkv.local_is_global.numpy().copy()
         out["prefill_next_free_block"] = np.int64(pkv.next_free_block)
         out["prefill_pool_sha"] = pool_digest(pkv, T, D)
+        if quest_budget is not None:
+            out["prefill_quest_min"], out["prefill_quest_max"] = quest_bounds(pkv, T)
+        rec = {}
         for s_ in range(n_decode):
             for l in range(Ly):
                 q, k, v, pk = dec[s_][l]
                 gp = gps[l]
-                sf = make_self(m, cfg, l, gp, prefill_stub, t.flash_attn_with_kvcache_ref)
+                sf = make_self(m, cfg, l, gp, prefill_stub, t.flash_attn_with_kvcache_ref, record=rec)
                 if defer:
                     g = None
                 else:
@@ -220,6 +229,9 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
                     out[f"d{s_}_l{l}_scores"] = O.bf16_bits(nb(g))[0]
                 o = m.self_attn_forward_patch_inference(sf, pkv, (1, 1), tb(q), tb(pk), tb(k), tb(v), g)
                 out[f"d{s_}_l{l}_out"] = nb(o)[0, 0]
+                if quest_budget is not None:  # what quest_select_blocks handed to the decode kernel
+                    out[f"d{s_}_l{l}_qsl"] = rec["seqlens"].numpy()[0]
+                    out[f"d{s_}_l{l}_qbt"] = rec["table"].numpy()[0]
             out[f"d{s_}_block_table"] = pkv.block_table.numpy().copy()
             out[f"d{s_}_global_lengths"] = pkv.global_lengths.numpy().copy()
             out[f"d{s_}_local_is_global"] = pkv.local_is_global.numpy().copy()
@@ -227,9 +239,11 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
             out[f"d{s_}_local_ptr"] = np.int64(pkv.local_ptr)
             out[f"d{s_}_local_length"] = np.int64(pkv.local_length)
             out[f"d{s_}_pool_sha"] = pool_digest(pkv, T, D)
+        if quest_budget is not None:
+            out["final_quest_min"], out["final_quest_max"] = quest_bounds(pkv, T)
     meta = dict(Ly=Ly, L=L, Hq=Hq, Hk=Hk, D=D, W=W, T=T, inner=inner, threshold=threshold, n_decode=n_decode,
                 defer=int(defer), seed=seed, max_total_tokens=max_total_tokens, max_tokens_per_head=max_tokens_per_head,
-                rows_out=rows_out)
+                rows_out=rows_out, quest_budget=quest_budget if quest_budget is not None else -1)
     for kk_, vv_ in meta.items():
         out[f"meta_{kk_}"] = np.float64(vv_)
     out["meta_inputs"] = np.array(list(inputs))
@@ -241,6 +255,19 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
         out[f"l{l}_b2"] = O.bf16_bits(p.b2)
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
     print(name, "written", {k_: v_.shape for k_, v_ in out.items() if k_.startswith("prefill")})
+
+
+def quest_bounds(pkv, T):
+    """bf16 bits of quest_block_key_min / _max of every live global page, in (layer, head, page) order."""
+    Ly, Hk, _ = pkv.block_table.shape
+    W = pkv.local_is_global.shape[-1]
+    pages = []
+    for l in range(Ly):
+        for h in range(Hk):
+            n = (int(pkv.global_lengths[l, h]) + T - 1) // T
+            pages += [int(x) for x in pkv.block_table[l, h, W // T:W // T + n]]
+    idx = torch.tensor(pages, dtype=torch.long)
+    return (O.bf16_bits(nb(pkv.quest_block_key_min[idx])), O.bf16_bits(nb(pkv.quest_block_key_max[idx])))
 
 
 def pool_digest(pkv, T, D):
@@ -388,6 +415,9 @@ def main():
     if os.environ.get("WGKV_GOLDEN_ONLY") == "gate_ckpt":
         gate_checkpoint_case(m)
         return
+    if os.environ.get("WGKV_GOLDEN_ONLY") == "quest":
+        quest_case(m, t)
+        return
     gate_checkpoint_case(m)
     decode_cases(t)
     indices_cases(m)
@@ -409,6 +439,15 @@ def main():
                       rates=[0.4, 0.2], threshold=0.5, n_decode=140, defer=True, seed=3,
                       max_total_tokens=2 * 2 * 400, max_tokens_per_head=400, rows_out=8,
                       inputs=("pre_k", "post_k"), act="silu")
+    quest_case(m, t)
+
+
+def quest_case(m, t):
+    # QUEST block selection over the paged pool (use_quest, :452-576, page bounds :744-761, :1333-1347):
+    # global pages grow by promotion while the token budget keeps only part of them.
+    run_pipeline_case(m, t, "quest_small", Ly=2, L=400, Hq=8, Hk=2, D=64, W=64, T=16, inner=32,
+                      rates=[0.45, 0.7], threshold=0.5, n_decode=48, defer=False, seed=4,
+                      max_total_tokens=2 * 2 * 600, max_tokens_per_head=600, rows_out=8, quest_budget=64 + 80)
 
 
 if __name__ == "__main__":

@@ -38,6 +38,7 @@ class PipelineCase:
         self.seed = g("seed")
         self.max_total_tokens, self.max_tokens_per_head = g("max_total_tokens"), g("max_tokens_per_head")
         self.rows_out = g("rows_out")
+        self.quest_budget = g("quest_budget") if "meta_quest_budget" in z else -1
         self.threshold = float(z["meta_threshold"])
         self.inputs = tuple(str(x) for x in z["meta_inputs"])
         self.act = str(z["meta_act"])
@@ -83,7 +84,29 @@ class PipelineCase:
     def new_state(self):
         return O.PoolState(layers=self.Ly, batch=1, kv_heads=self.Hk, head_dim=self.D, window=self.W, page=self.T,
                            max_total_tokens=self.max_total_tokens, max_tokens_per_head=self.max_tokens_per_head,
-                           defer=self.defer)
+                           defer=self.defer, quest=self.quest_budget >= 0)
+
+
+def quest_sets_agree(st, l, b, h, q_group, got_pages, ref_pages):
+    """Selected page sets of one (layer, b, h) agree up to pages whose score ties the lowest chosen
+    full-page score (their order is torch.topk's to choose).  Pages are physical ids, ring pages and
+    the trailing partial page included."""
+    got, ref = set(int(x) for x in got_pages), set(int(x) for x in ref_pages)
+    if got == ref:
+        return True
+    if len(got) != len(ref):
+        return False
+    T = st.page
+    full = int(st.global_lengths[l, b, h]) // T
+    row = st.block_table[l, b, h, st.local_pages:st.local_pages + full]
+    pos = {int(p): i for i, p in enumerate(row)}  # full global pages only
+    diff = got ^ ref
+    if not all(p in pos for p in diff):
+        return False
+    sc = st.quest_scores(l, b, h, q_group)
+    kth_got = min(sc[pos[p]] for p in got if p in pos)
+    kth_ref = min(sc[pos[p]] for p in ref if p in pos)
+    return kth_got == kth_ref and all(sc[pos[p]] == kth_got for p in diff)
 
 
 def regen_decode_inputs(params):

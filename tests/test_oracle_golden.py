@@ -115,3 +115,50 @@ def test_decode_steps_match_reference(case):
         dig = O.pool_digest(st.block_table, st.global_lengths, st.local_length,
                             O.bf16_bits(st.k), O.bf16_bits(st.v), st.page, st.window)
         assert np.array_equal(dig, z[f"d{s}_pool_sha"]), s
+
+
+def test_quest_selection_matches_reference():
+    """QUEST (use_quest): page key bounds after prefill and promotion, the selected pages and lengths
+    of quest_select_blocks, and the attention over them, against the reference run on CPU."""
+    from golden_cases import PipelineCase, quest_sets_agree
+    case = PipelineCase("quest_small")
+    st = case.new_state()
+    z = case.z
+    T, W = case.T, case.W
+
+    def live_bounds():
+        pages = []
+        for l in range(case.Ly):
+            for h in range(case.Hk):
+                n = (int(st.global_lengths[l, 0, h]) + T - 1) // T
+                pages += list(st.block_table[l, 0, h, W // T:W // T + n])
+        return O.bf16_bits(st.qmin[pages]), O.bf16_bits(st.qmax[pages])
+
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        st.prefill_layer(l, k, v, case.ref_mask(l), pre_key=pk)
+    mn, mx = live_bounds()
+    assert np.array_equal(mn, z["prefill_quest_min"]) and np.array_equal(mx, z["prefill_quest_max"])
+    partial = 0
+    for s in range(case.n_decode):
+        for l in range(case.Ly):
+            q, k, v, pk = case.decode[s][l]
+            if l == 0 and st.local_length == st.window:
+                st.promote()
+            gm = case.ref_decode_mask(s, l)
+            cur = st.append_layer(l, k[:, :, 0], v[:, :, 0], gm[:, :, 0])
+            sl, tables = st.quest_select(l, cur, q[:, :, 0], case.quest_budget)
+            assert np.array_equal(sl[0], z[f"d{s}_l{l}_qsl"]), (s, l)
+            for h in range(case.Hk):
+                n = (int(sl[0, h]) - cur + T - 1) // T + (cur + T - 1) // T
+                ref_pages = z[f"d{s}_l{l}_qbt"][h, :n]
+                assert quest_sets_agree(st, l, 0, h, q[0, h * case.G:(h + 1) * case.G, 0], tables[h], ref_pages), (s, l, h)
+                partial += n < (cur + T - 1) // T + (int(st.global_lengths[l, 0, h]) + T - 1) // T
+            # attention over the reference's choice (equal to ours up to tie order, checked above)
+            bt = z[f"d{s}_l{l}_qbt"][None].astype(np.int32)
+            kc, vc = st.paged_views()
+            o = O.paged_decode(q.transpose(0, 2, 1, 3), kc, vc, sl, bt, case.D ** -0.5)
+            np.testing.assert_allclose(o[0, 0], z[f"d{s}_l{l}_out"], atol=2e-2, rtol=1e-2)
+    assert partial > 0  # the budget left pages out
+    mn, mx = live_bounds()
+    assert np.array_equal(mn, z["final_quest_min"]) and np.array_equal(mx, z["final_quest_max"])

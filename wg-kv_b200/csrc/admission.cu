@@ -312,6 +312,30 @@ __global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs 
   }
 }
 
+// QUEST key bounds of the global pages a prefill just filled (:1333-1347): one warp per page,
+// lanes over the head dimension.
+__global__ void __launch_bounds__(256) quest_bounds_kernel(PoolArgs pa, int layer, const int* okflag) {
+  const wgkv_pool& P = pa.P;
+  if (!*okflag) return;
+  const int BH = P.batch * P.kv_heads, bh = blockIdx.y;
+  const int T = P.page, D = P.head_dim;
+  const int glen = P.global_lengths[int64_t(layer) * BH + bh];
+  const int pg = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (pg * T >= glen) return;
+  const int64_t pid = P.block_table[(int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / T + pg];
+  const int rows = min(T, glen - pg * T);
+  for (int c = lane; c < D; c += 32) {
+    uint16_t lo = P.k[pid * T * D + c], hi = lo;
+    for (int r = 1; r < rows; ++r) {
+      const uint16_t kb = P.k[(pid * T + r) * D + c];
+      if (bf2f(kb) < bf2f(lo)) lo = kb;
+      if (bf2f(kb) > bf2f(hi)) hi = kb;
+    }
+    P.quest_min[pid * D + c] = lo;
+    P.quest_max[pid * D + c] = hi;
+  }
+}
+
 // ============================================================================
 // decode: ring append + cache_seqlens
 // ============================================================================
@@ -430,6 +454,22 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
     for (int c = 0; c < D / 8; ++c) {
       kd[c] = ks[c];
       vd[c] = vs[c];
+    }
+    if (P.quest_min) {  // page key bounds (:744-761): a new page starts at the key
+      uint16_t* mn = P.quest_min + int64_t(pid) * D;
+      uint16_t* mx = P.quest_max + int64_t(pid) * D;
+      const uint16_t* kk = P.k + src * D;
+      for (int c = 0; c < D; ++c) {
+        const uint16_t kb = kk[c];
+        if (gl % T == 0) {
+          mn[c] = kb;
+          mx[c] = kb;
+        } else {
+          const float x = bf2f(kb);
+          if (x < bf2f(mn[c])) mn[c] = kb;
+          if (x > bf2f(mx[c])) mx[c] = kb;
+        }
+      }
     }
     P.global_lengths[i] = gl + 1;
   }
@@ -723,6 +763,10 @@ extern "C" int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len,
   else
     prefill_scatter_kernel<false><<<grid, kScanThreads, 0, s>>>(pa, layer, seq_len, n_early, n_loc, nch, mv, K, V, PK,
                                                                 counts, first, okflag);
+  if (pool->quest_min && pool->quest_max && n_early > 0) {
+    const int max_pages = (n_early + pool->page - 1) / pool->page;
+    quest_bounds_kernel<<<dim3((max_pages + 7) / 8, BH), 256, 0, s>>>(pa, layer, okflag);
+  }
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 

@@ -18,6 +18,7 @@ from .layers import (  # noqa: F401
     decode_wrapper,
     migrate_local_kv_to_global,
     prefill_wrapper,
+    quest_select_blocks,
     refresh_local_is_global,
     self_attn_forward_patch,
     self_attn_decode_fused,

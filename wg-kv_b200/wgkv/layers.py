@@ -40,7 +40,8 @@ def _maybe_init(self, past_key_value, batch_size, key_states):
         init_pool(past_key_value, layers=c.num_hidden_layers, batch=batch_size, kv_heads=c.num_key_value_heads,
                   head_dim=self.head_dim, window=c.local_window_size, page=c.block_size,
                   max_total_tokens=c.max_total_tokens, max_tokens_per_head=c.max_tokens_per_head,
-                  device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)))
+                  device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)),
+                  quest=bool(getattr(c, "use_quest", False)))
     elif self.layer_idx == 0:
         raise AssertionError("prefill on an initialised cache (the reference asserts the same, :1197)")
 
@@ -148,9 +149,39 @@ def decode_wrapper(self, past_key_value, query_states, pre_key, key_states, valu
     T = c.block_size
     k_cache = past_key_value.block_pool_k.view(past_key_value.total_blocks, T, self.head_dim)
     v_cache = past_key_value.block_pool_v.view(past_key_value.total_blocks, T, self.head_dim)
-    handle = self.decode_kernel_handle(query_states.transpose(1, 2), k_cache, v_cache, past_key_value.cache_seqlens,
-                                       past_key_value.block_table[l], self.scaling)
+    if getattr(c, "use_quest", False):
+        cache_seqlens, block_table = quest_select_blocks(self, query_states, past_key_value, local_blocks_per_head,
+                                                         device, RING_ON_DEVICE if dr else cur)
+    else:
+        cache_seqlens, block_table = past_key_value.cache_seqlens, past_key_value.block_table[l]
+    handle = self.decode_kernel_handle(query_states.transpose(1, 2), k_cache, v_cache, cache_seqlens, block_table,
+                                       self.scaling)
     return self.decode_kernel_executor(handle)
+
+
+def quest_select_blocks(self, query_states, past_key_value, local_blocks_per_head, device, local_tokens_total):
+    """QUEST page selection (:452-576) on the device (``wgkv_quest_select``), batched.
+
+    query_states (B, Hq, 1, D).  Returns (cache_seqlens (B, Hk) int32, block_table (B, Hk, S) int32):
+    the ring pages, the best full global pages by their key-bound score within
+    ``config.quest_token_budget`` (ties to the lower position) and the trailing partial page, in
+    position order (the reference lists the full pages in score order; attention does not depend on
+    it).  ``local_tokens_total`` may be ``RING_ON_DEVICE`` (-1) under graph capture."""
+    c = _cfg(self)
+    assert c.quest_token_budget is not None
+    s = past_key_value.wgkv_pool
+    B, Hq, _, D = query_states.shape
+    q = query_states[:, :, 0]
+    if q.stride(1) != D or q.stride(2) != 1:
+        q = q.contiguous()
+    stride = int(lib.wgkv_quest_table_stride(s.window, s.page, int(c.quest_token_budget), s.max_blocks_per_head))
+    seqlens = torch.empty(B, s.kv_heads, dtype=torch.int32, device=device)
+    table = torch.empty(B, s.kv_heads, stride, dtype=torch.int32, device=device)
+    st = lib.wgkv_quest_select(pool_ref(past_key_value), self.layer_idx, int(local_tokens_total), q.data_ptr(),
+                               q.stride(0), Hq, int(c.quest_token_budget), seqlens.data_ptr(), table.data_ptr(),
+                               stride, stream_ptr(device))
+    check(st, "wgkv_quest_select")
+    return seqlens, table
 
 
 def _append(self, past_key_value, l, insert_pos, cur, pre_key, key_states, value_states, defer, device):

@@ -39,11 +39,13 @@ class WgkvPool(ctypes.Structure):
         ("max_blocks_per_head", ctypes.c_int32),
         ("max_tokens_per_head", ctypes.c_int32),
         ("ring_state", ctypes.c_void_p),
+        ("quest_min", ctypes.c_void_p),
+        ("quest_max", ctypes.c_void_p),
     ]
 
 
 def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_total_tokens, max_tokens_per_head,
-              device, dtype=torch.bfloat16, defer=False):
+              device, dtype=torch.bfloat16, defer=False, quest=False):
     """Allocate the pool on ``cache`` (any attribute holder), as prefill_wrapper does at layer 0."""
     assert window % page == 0, "local_window_size must be a multiple of block_size"
     local_pages = window // page
@@ -75,6 +77,9 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     # device copy of (local_length, local_ptr), used when a decode step runs as a CUDA graph
     cache.ring_state = torch.zeros(2, dtype=torch.int32, device=dev)
     cache.wgkv_device_ring = False
+    if quest:  # per-page key bounds for QUEST selection (modeling_layers.py:1232-1240)
+        cache.quest_block_key_min = torch.zeros(total_blocks, head_dim, dtype=dtype, device=dev)
+        cache.quest_block_key_max = torch.zeros(total_blocks, head_dim, dtype=dtype, device=dev)
     s = WgkvPool()
     s.k = cache.block_pool_k.data_ptr()
     s.v = cache.block_pool_v.data_ptr()
@@ -89,6 +94,8 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     s.window, s.page = window, page
     s.max_blocks_per_head, s.max_tokens_per_head = max_blocks_per_head, max_tokens_per_head
     s.ring_state = cache.ring_state.data_ptr()
+    s.quest_min = cache.quest_block_key_min.data_ptr() if quest else None
+    s.quest_max = cache.quest_block_key_max.data_ptr() if quest else None
     cache.wgkv_pool = s
     cache.gated_kv_initialized = True
     return cache
