@@ -27,6 +27,7 @@
  *   wgkv_sparse_prefill       sparse_attn_func (vLLM fork) as called at :1366-1374
  *   wgkv_quest_select         quest_select_blocks :452-576 (page bounds kept by prefill :1333-1347 and
  *                             promotion :744-761)
+ *   wgkv_snapkv_evict         snapkv_evict :595-671 (free list reused by promotion :694-709)
  *   wgkv_paged_decode         flash_attn_with_kvcache_wrapper_triton_handle + split/reduce kernels :818-1140
  *                             (and the batched flash_attn_with_kvcache_wrapper :766-811)
  */
@@ -84,6 +85,9 @@ WGKV_API int wgkv_num_sms(void);
  *   quest_min/max    optional (total_blocks, head_dim) bf16: element-wise min / max of the keys of every
  *                    global page (quest_block_key_min / _max, :1232-1240), kept by wgkv_prefill_admit and
  *                    wgkv_promote when set; read by wgkv_quest_select.  NULL = QUEST off.
+ *   free_ids/count   optional SnapKV free list (free_block_ids, :1262): device int32[total_blocks] and its
+ *                    device length.  wgkv_snapkv_evict appends the pages it empties; wgkv_promote takes
+ *                    new pages from the list's tail first (:694-709).  NULL = no free list.
  * The ring slot s of (layer l, batch b, head h) is pool row ((l*batch + b)*kv_heads + h)*window + s.
  */
 typedef struct wgkv_pool {
@@ -107,6 +111,8 @@ typedef struct wgkv_pool {
   int32_t* ring_state;
   uint16_t* quest_min;
   uint16_t* quest_max;
+  int32_t* free_ids;
+  int32_t* free_count;
 } wgkv_pool;
 
 /* insert_pos / local_ptr value that means "read the position from pool->ring_state". */
@@ -233,6 +239,23 @@ WGKV_API size_t wgkv_quest_table_stride(int window, int page, int token_budget, 
 WGKV_API int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local_len, const uint16_t* q, int64_t q_sb,
                                int q_heads, int token_budget, int32_t* out_seqlens, int32_t* out_table,
                                int64_t out_stride, void* stream);
+
+/* ---- SnapKV eviction (snapkv_enabled) ------------------------------------- */
+/*
+ * snapkv_evict (:595-671) for every (layer, b, h): scores each global token by the softmax attention
+ * of the recorded window queries (bf16(bf16(q . k) * scale), fp32 softmax), max over the head's G
+ * query heads, mean over the window, max-pooled with the odd kernel_size; evicts the
+ * int(glen * evict_ratio) lowest (ties: lower positions first), packs the kept tokens to the front
+ * of the head's pages, returns emptied pages to the free list in (layer, b, h) order (their table
+ * entries become total_blocks - 1) and shrinks global_lengths.  queries (layers, batch, window,
+ * q_heads, head_dim) bf16 -- the snapkv_query_buffer of :1255-1258 with a batch axis.  Requires
+ * pool->free_ids; G = q_heads / kv_heads must divide 16 and window * G must be a multiple of 16.
+ * The caller decides when (the reference: total global tokens > snapkv_max_cached_tokens, :1502-1507).
+ */
+WGKV_API size_t wgkv_snapkv_workspace_size(const wgkv_pool* pool, int window, int q_heads);
+WGKV_API int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries, int window, int q_heads,
+                               float softmax_scale, double evict_ratio, int kernel_size, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* ---- decoder plumbing of the end-to-end driver (no reference counterpart on the hot path) ---- */
 /*

@@ -381,6 +381,8 @@ class PoolState:
     max_tokens_per_head: int
     defer: bool = False
     quest: bool = False
+    snapkv: tuple | None = None  # (max_cached_tokens, evict_ratio, window, kernel_size)
+    q_heads: int = 0             # needed with snapkv (query buffer)
 
     def __post_init__(self):
         assert self.window % self.page == 0
@@ -399,6 +401,13 @@ class PoolState:
         self.local_ptr = 0
         self.local_length = 0
         self.next_free_block = Ly * B * Hk * self.local_pages
+        if self.snapkv is not None:  # modeling_layers.py:1249-1262, with a batch axis
+            win = self.snapkv[2]
+            self.snap_q = np.zeros((Ly, B, win, self.q_heads, self.head_dim), np.float32)
+            self.snap_len = 0
+            self.snap_ptr = 0
+            self.evict_count = 0
+            self.free = []
         if self.quest:  # per-page key bounds (quest_block_key_min / _max, modeling_layers.py:1232-1240)
             self.qmin = np.zeros((self.total_blocks, self.head_dim), np.float32)
             self.qmax = np.zeros((self.total_blocks, self.head_dim), np.float32)
@@ -462,12 +471,16 @@ class PoolState:
         need = off == 0
         nnew = int(need.sum())
         if nnew:
-            if self.next_free_block + nnew > self.total_blocks:
+            nff = min(nnew, len(self.free)) if self.snapkv is not None else 0
+            ids = self.free[len(self.free) - nff:] if nff else []  # :694-709: the free list's tail first
+            if nff:
+                self.free = self.free[:len(self.free) - nff]
+            if self.next_free_block + nnew - nff > self.total_blocks:
                 raise PoolError("Allocation exceeds total_blocks")
+            ids = list(ids) + list(range(self.next_free_block, self.next_free_block + nnew - nff))
             sel = flat[need]
-            self.block_table[sel[:, 0], sel[:, 1], sel[:, 2], gblk[need]] = np.arange(
-                self.next_free_block, self.next_free_block + nnew)
-            self.next_free_block += nnew
+            self.block_table[sel[:, 0], sel[:, 1], sel[:, 2], gblk[need]] = np.array(ids, np.int32)
+            self.next_free_block += nnew - nff
         src = np.array([self.ring_row(l, b, h, ptr) for l, b, h in flat])
         phys = self.block_table[flat[:, 0], flat[:, 1], flat[:, 2], gblk].astype(np.int64)
         dst = phys * T + off
@@ -517,6 +530,82 @@ class PoolState:
     def decode_tables(self, l, cur_local_len):
         """``cache_seqlens``/``block_table`` views of modeling_layers.py:1429-1436."""
         return (cur_local_len + self.global_lengths[l]).astype(np.int32), self.block_table[l]
+
+    # -- SnapKV (modeling_layers.py:579-671) ------------------------------------------------------
+    def snap_record(self, l, q):
+        """snapkv_record_queries (:579-592): q ``(B, Hq, Lq, D)`` (post-RoPE queries of layer l)."""
+        win = self.snapkv[2]
+        Lq = q.shape[2]
+        if Lq > 1:
+            take = min(win, Lq)
+            self.snap_q[l, :, :take] = np.transpose(q[:, :, Lq - take:], (0, 2, 1, 3))
+            if l == self.layers - 1:
+                self.snap_len = take
+                self.snap_ptr = take % win
+        else:
+            self.snap_q[l, :, self.snap_ptr] = q[:, :, 0]
+            if l == self.layers - 1:
+                self.snap_len = min(win, self.snap_len + 1)
+                self.snap_ptr = (self.snap_ptr + 1) % win
+
+    def snap_should_evict(self):
+        """The trigger of :1500-1507 (checked after the last layer)."""
+        return int(self.global_lengths.sum()) > self.snapkv[0]
+
+    def snap_scores(self, l, b, h, scale):
+        """head_scores of snapkv_evict (:611-625): softmax over the head's global keys of each window
+        query (scores rounded to bf16, then scaled in bf16), max over the group, mean over the
+        window, max-pooled with the odd kernel (padding kernel // 2)."""
+        T, win, ks = self.page, self.snapkv[2], self.snapkv[3]
+        glen = int(self.global_lengths[l, b, h])
+        G = self.q_heads // self.kv_heads
+        q = self.snap_q[l, b][:, h * G:(h + 1) * G]                         # (win, G, D)
+        pos = np.arange(glen)
+        rows = self.block_table[l, b, h, self.local_pages + pos // T].astype(np.int64) * T + pos % T
+        keys = self.k[rows]                                                   # (glen, D)
+        att = bf16(bf16((np.transpose(q, (1, 0, 2)).astype(np.float64) @ keys.T.astype(np.float64)).astype(np.float32))
+                   * np.float32(scale))                                       # (G, win, glen)
+        att = att - att.max(-1, keepdims=True)
+        e = np.exp(att.astype(np.float64))
+        p = (e / e.sum(-1, keepdims=True)).astype(np.float32)
+        sc = p.max(0).astype(np.float64).mean(0).astype(np.float32)          # (glen,)
+        pad = ks // 2
+        padded = np.concatenate([np.full(pad, -np.inf, np.float32), sc, np.full(pad, -np.inf, np.float32)])
+        return np.lib.stride_tricks.sliding_window_view(padded, ks).max(-1).astype(np.float32)
+
+    def snap_evict(self, scale, override=None):
+        """snapkv_evict (:595-671) for every (layer, b, h).  The num_evict lowest-scored global tokens
+        go, ties to the lower positions (the reference's torch.topk leaves their order open);
+        ``override[(l, b, h)]`` = positions to evict instead.  Kept tokens are packed to the front of
+        the head's pages, freed pages go to the free list in (layer, b, h) order."""
+        T, ratio = self.page, self.snapkv[1]
+        self.evict_count += 1
+        for l in range(self.layers):
+            for b in range(self.batch):
+                for h in range(self.kv_heads):
+                    glen = int(self.global_lengths[l, b, h])
+                    n_ev = int(glen * ratio)
+                    if n_ev == 0:
+                        continue
+                    if override is not None:
+                        ev = np.asarray(override[(l, b, h)])
+                    else:
+                        sc = self.snap_scores(l, b, h, scale)
+                        ev = np.lexsort((np.arange(glen), sc.astype(np.float64)))[:n_ev]
+                    keep = np.setdiff1d(np.arange(glen), ev)
+                    nb_old = (glen + T - 1) // T
+                    nb_new = (len(keep) + T - 1) // T
+                    tab = self.block_table[l, b, h, self.local_pages:self.local_pages + nb_old].astype(np.int64)
+                    rows = tab[np.arange(glen) // T] * T + np.arange(glen) % T
+                    if len(keep):
+                        kk, vv = self.k[rows[keep]].copy(), self.v[rows[keep]].copy()
+                        self.k[rows[:len(keep)]] = kk
+                        self.v[rows[:len(keep)]] = vv
+                    if nb_new < nb_old:
+                        self.free.extend(int(x) for x in tab[nb_new:])
+                        self.block_table[l, b, h, self.local_pages + nb_new:self.local_pages + nb_old] = \
+                            self.total_blocks - 1
+                    self.global_lengths[l, b, h] = len(keep)
 
     def quest_scores(self, l, b, h, q):
         """Block scores of quest_select_blocks (:495-504) for the head's full and partial global pages:

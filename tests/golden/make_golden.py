@@ -155,7 +155,7 @@ def make_self(m, cfg, layer_idx, gp, prefill_stub, decode_ref, record=None):
 
 def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, threshold,
                       n_decode, defer, seed, max_total_tokens, max_tokens_per_head, rows_out=16,
-                      inputs=("pre_k",), act="gelu", quest_budget=None):
+                      inputs=("pre_k",), act="gelu", quest_budget=None, snapkv=None):
     """Prefill of one sequence through every layer, then n_decode decode steps."""
     rng = np.random.default_rng(seed)
     G = Hq // Hk
@@ -182,8 +182,24 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
     cfg = SimpleNamespace(num_hidden_layers=Ly, num_key_value_heads=Hk, num_attention_heads=Hq, head_dim=D,
                           block_size=T, max_total_tokens=max_total_tokens, max_tokens_per_head=max_tokens_per_head,
                           local_window_size=W, use_quest=quest_budget is not None,
-                          quest_token_budget=quest_budget, g_defer=defer, snapkv_enabled=False,
+                          quest_token_budget=quest_budget, g_defer=defer, snapkv_enabled=snapkv is not None,
                           use_baseline=False, g_threshold=threshold, g_expand=inner / D, random_sparsity=None)
+    if snapkv is not None:
+        cfg.snapkv_max_cached_tokens, cfg.snapkv_evict_ratio, cfg.snapkv_window_size, cfg.snapkv_kernel_size = snapkv
+    evictions = []  # per eviction: list over (layer, head) of (head_scores, evicted positions)
+    real_topk = torch.topk
+
+    def recording_topk(x, k, *a, largest=True, **kw):
+        r = real_topk(x, k, *a, largest=largest, **kw)
+        if not largest and snapkv is not None:
+            evictions[-1].append((x.detach().clone(), r.indices.clone()))
+        return r
+
+    real_evict = m.snapkv_evict
+
+    def recording_evict(*a, **kw):
+        evictions.append([])
+        return real_evict(*a, **kw)
     pkv = SimpleNamespace()
     captured = {}
 
@@ -196,6 +212,8 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
         return torch.zeros_like(qt)
 
     gps = []
+    m.snapkv_evict = recording_evict
+    torch.topk = recording_topk
     with torch.no_grad():
         for l in range(Ly):
             q, k, v, pk = per_layer[l]
@@ -239,11 +257,24 @@ def run_pipeline_case(m, t, name, *, Ly, L, Hq, Hk, D, W, T, inner, rates, thres
             out[f"d{s_}_local_ptr"] = np.int64(pkv.local_ptr)
             out[f"d{s_}_local_length"] = np.int64(pkv.local_length)
             out[f"d{s_}_pool_sha"] = pool_digest(pkv, T, D)
+            if snapkv is not None:
+                out[f"d{s_}_free_ids"] = np.array(pkv.free_block_ids, np.int64)
+                out[f"d{s_}_evict_count"] = np.int64(pkv.snapkv_evict_count)
         if quest_budget is not None:
             out["final_quest_min"], out["final_quest_max"] = quest_bounds(pkv, T)
+    torch.topk = real_topk
+    m.snapkv_evict = real_evict
+    if snapkv is not None:
+        out["snap_n_evictions"] = np.int64(len(evictions))
+        for e, ev in enumerate(evictions):
+            for j, (sc, idx) in enumerate(ev):
+                out[f"snap_e{e}_{j}_scores"] = sc.numpy().astype(np.float32)
+                out[f"snap_e{e}_{j}_evict"] = idx.numpy().astype(np.int64)
     meta = dict(Ly=Ly, L=L, Hq=Hq, Hk=Hk, D=D, W=W, T=T, inner=inner, threshold=threshold, n_decode=n_decode,
                 defer=int(defer), seed=seed, max_total_tokens=max_total_tokens, max_tokens_per_head=max_tokens_per_head,
                 rows_out=rows_out, quest_budget=quest_budget if quest_budget is not None else -1)
+    if snapkv is not None:
+        meta.update(snap_max=snapkv[0], snap_ratio=snapkv[1], snap_window=snapkv[2], snap_kernel=snapkv[3])
     for kk_, vv_ in meta.items():
         out[f"meta_{kk_}"] = np.float64(vv_)
     out["meta_inputs"] = np.array(list(inputs))
@@ -415,6 +446,9 @@ def main():
     if os.environ.get("WGKV_GOLDEN_ONLY") == "gate_ckpt":
         gate_checkpoint_case(m)
         return
+    if os.environ.get("WGKV_GOLDEN_ONLY") == "snapkv":
+        snapkv_case(m, t)
+        return
     if os.environ.get("WGKV_GOLDEN_ONLY") == "quest":
         quest_case(m, t)
         return
@@ -440,6 +474,7 @@ def main():
                       max_total_tokens=2 * 2 * 400, max_tokens_per_head=400, rows_out=8,
                       inputs=("pre_k", "post_k"), act="silu")
     quest_case(m, t)
+    snapkv_case(m, t)
 
 
 def quest_case(m, t):
@@ -448,6 +483,16 @@ def quest_case(m, t):
     run_pipeline_case(m, t, "quest_small", Ly=2, L=400, Hq=8, Hk=2, D=64, W=64, T=16, inner=32,
                       rates=[0.45, 0.7], threshold=0.5, n_decode=48, defer=False, seed=4,
                       max_total_tokens=2 * 2 * 600, max_tokens_per_head=600, rows_out=8, quest_budget=64 + 80)
+
+
+
+def snapkv_case(m, t):
+    # SnapKV eviction (snapkv_enabled, :579-671) with the free list it feeds (:694-709): the cache
+    # limit is crossed repeatedly while promotions grow the global pages.
+    run_pipeline_case(m, t, "snapkv_small", Ly=2, L=400, Hq=8, Hk=2, D=64, W=64, T=16, inner=32,
+                      rates=[0.45, 0.7], threshold=0.5, n_decode=60, defer=False, seed=5,
+                      max_total_tokens=2 * 2 * 700, max_tokens_per_head=700, rows_out=8,
+                      snapkv=(600, 0.3, 32, 5))
 
 
 if __name__ == "__main__":

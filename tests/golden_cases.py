@@ -39,6 +39,8 @@ class PipelineCase:
         self.max_total_tokens, self.max_tokens_per_head = g("max_total_tokens"), g("max_tokens_per_head")
         self.rows_out = g("rows_out")
         self.quest_budget = g("quest_budget") if "meta_quest_budget" in z else -1
+        self.snapkv = ((g("snap_max"), float(z["meta_snap_ratio"]), g("snap_window"), g("snap_kernel"))
+                       if "meta_snap_max" in z else None)
         self.threshold = float(z["meta_threshold"])
         self.inputs = tuple(str(x) for x in z["meta_inputs"])
         self.act = str(z["meta_act"])
@@ -84,7 +86,7 @@ class PipelineCase:
     def new_state(self):
         return O.PoolState(layers=self.Ly, batch=1, kv_heads=self.Hk, head_dim=self.D, window=self.W, page=self.T,
                            max_total_tokens=self.max_total_tokens, max_tokens_per_head=self.max_tokens_per_head,
-                           defer=self.defer, quest=self.quest_budget >= 0)
+                           defer=self.defer, quest=self.quest_budget >= 0, snapkv=self.snapkv, q_heads=self.Hq)
 
 
 def quest_sets_agree(st, l, b, h, q_group, got_pages, ref_pages):
@@ -107,6 +109,19 @@ def quest_sets_agree(st, l, b, h, q_group, got_pages, ref_pages):
     kth_got = min(sc[pos[p]] for p in got if p in pos)
     kth_ref = min(sc[pos[p]] for p in ref if p in pos)
     return kth_got == kth_ref and all(sc[pos[p]] == kth_got for p in diff)
+
+
+def snap_evicted_agree(scores, got, ref):
+    """Evicted position sets agree up to positions whose (pooled) score ties the highest evicted
+    score in both: torch.topk(largest=False) leaves the order of equal scores open."""
+    got, ref = set(int(x) for x in got), set(int(x) for x in ref)
+    if got == ref:
+        return True
+    if len(got) != len(ref):
+        return False
+    thr_g = max(scores[list(got)])
+    thr_r = max(scores[list(ref)])
+    return thr_g == thr_r and all(scores[p] == thr_g for p in got ^ ref)
 
 
 def regen_decode_inputs(params):

@@ -162,3 +162,64 @@ def test_quest_selection_matches_reference():
     assert partial > 0  # the budget left pages out
     mn, mx = live_bounds()
     assert np.array_equal(mn, z["final_quest_min"]) and np.array_equal(mx, z["final_quest_max"])
+
+
+def test_snapkv_eviction_matches_reference():
+    """SnapKV (snapkv_enabled): query window, head scores, evicted sets (up to tied scores), front
+    compaction, freed pages and their reuse by promotion, against the reference run on CPU."""
+    from golden_cases import PipelineCase, snap_evicted_agree
+    case = PipelineCase("snapkv_small")
+    st = case.new_state()
+    z = case.z
+    scale = case.D ** -0.5
+    n_ev = [0]
+
+    def evict():
+        e = n_ev[0]
+        n_ev[0] += 1
+        override, j = {}, 0
+        for l in range(case.Ly):
+            for h in range(case.Hk):
+                glen = int(st.global_lengths[l, 0, h])
+                if int(glen * case.snapkv[1]) == 0:
+                    continue
+                ref_sc = z[f"snap_e{e}_{j}_scores"]
+                ref_ev = z[f"snap_e{e}_{j}_evict"]
+                sc = st.snap_scores(l, 0, h, scale)
+                np.testing.assert_allclose(sc, ref_sc, rtol=1e-5, atol=1e-8)
+                mine = np.lexsort((np.arange(glen), sc.astype(np.float64)))[:len(ref_ev)]
+                assert snap_evicted_agree(ref_sc, mine, ref_ev), (e, l, h)
+                override[(l, 0, h)] = ref_ev
+                j += 1
+        st.snap_evict(scale, override=override)
+
+    for l in range(case.Ly):
+        q, k, v, pk = case.prefill[l]
+        st.prefill_layer(l, k, v, case.ref_mask(l), pre_key=pk)
+        st.snap_record(l, q)
+        if l == case.Ly - 1 and st.snap_should_evict():
+            evict()
+    assert np.array_equal(st.block_table[:, 0], z["prefill_block_table"])
+    assert np.array_equal(st.global_lengths[:, 0], z["prefill_global_lengths"])
+    for s in range(case.n_decode):
+        for l in range(case.Ly):
+            q, k, v, pk = case.decode[s][l]
+            if l == 0 and st.local_length == st.window:
+                st.promote()
+            cur = st.append_layer(l, k[:, :, 0], v[:, :, 0], case.ref_decode_mask(s, l)[:, :, 0])
+            sl, bt = st.decode_tables(l, cur)
+            kc, vc = st.paged_views()
+            o = O.paged_decode(q.transpose(0, 2, 1, 3), kc, vc, sl, bt, scale)
+            np.testing.assert_allclose(o[0, 0], z[f"d{s}_l{l}_out"], atol=2e-2, rtol=1e-2)
+            st.snap_record(l, q)
+            if l == case.Ly - 1 and st.snap_should_evict():
+                evict()
+        assert np.array_equal(st.block_table[:, 0], z[f"d{s}_block_table"]), s
+        assert np.array_equal(st.global_lengths[:, 0], z[f"d{s}_global_lengths"]), s
+        assert st.next_free_block == int(z[f"d{s}_next_free_block"]), s
+        assert st.free == [int(x) for x in z[f"d{s}_free_ids"]], s
+        assert st.evict_count == int(z[f"d{s}_evict_count"]), s
+        dig = O.pool_digest(st.block_table, st.global_lengths, st.local_length,
+                            O.bf16_bits(st.k), O.bf16_bits(st.v), st.page, st.window)
+        assert np.array_equal(dig, z[f"d{s}_pool_sha"]), s
+    assert n_ev[0] == int(z["snap_n_evictions"]) == 2

@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
   const int per = (N + kPromoteThreads - 1) / kPromoteThreads;
   const int i0 = threadIdx.x * per;  // contiguous entries keep the (layer, b, h) allocation order
   __shared__ int wsum[kPromoteThreads / 32];
-  __shared__ int s_ovf, s_nf, s_ok;
+  __shared__ int s_ovf, s_nf, s_ok, s_fc, s_nff;
   if (threadIdx.x == 0) s_ovf = 0;
   // all loads of this thread's entries are issued together; admission bits kept as a bitmask
   uint32_t fmask = 0;
@@ -418,20 +418,26 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
   }
   if (threadIdx.x == 0) {
     const int nf = *P.next_free_block;
+    // pages freed by eviction are reused first, the free list's tail in list order (:694-709)
+    const int fc = P.free_count ? *P.free_count : 0;
+    const int nff = tot < fc ? tot : fc;
     s_nf = nf;
+    s_fc = fc;
+    s_nff = nff;
     s_ok = 0;
     if (s_ovf) {
       set_error(P.err, WGKV_ERR_HEAD_CAPACITY);
-    } else if (int64_t(nf) + tot > P.total_blocks) {
+    } else if (int64_t(nf) + tot - nff > P.total_blocks) {
       set_error(P.err, WGKV_ERR_POOL_EXHAUSTED);
     } else {
-      *P.next_free_block = nf + tot;
+      *P.next_free_block = nf + tot - nff;
+      if (nff) *P.free_count = fc - nff;
       s_ok = 1;
     }
   }
   __syncthreads();
   if (!s_ok) return;
-  int next = s_nf + wb + x - need;
+  int next = wb + x - need;  // allocation rank of this thread's first new page
 #pragma unroll 1
   for (int k = 0; k < kPromoteMaxPer; ++k) {
     if (!(fmask & (1u << k))) continue;
@@ -440,7 +446,8 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
     int32_t* trow = P.block_table + int64_t(i) * P.max_blocks_per_head + W / T;
     int pid;
     if (gl % T == 0) {
-      pid = next++;
+      const int r = next++;
+      pid = r < s_nff ? P.free_ids[s_fc - s_nff + r] : s_nf + (r - s_nff);
       trow[gl / T] = pid;
     } else {
       pid = trow[gl / T];

@@ -1,0 +1,469 @@
+// SnapKV eviction over the paged pool (reference: snapkv_evict, src/modeling_layers.py:595-671),
+// for every (layer, sequence, KV head) at once.
+//
+// Per head: the window of recorded queries (win x G rows, post-RoPE) attends to the head's global
+// keys; each key's score is the max over the G query heads of its softmax probability, averaged
+// over the window, then max-pooled (odd kernel, padding kernel / 2).  The int(glen * ratio) lowest
+// pooled scores are evicted (ties: lower positions first -- torch.topk leaves their order open),
+// the kept tokens are packed to the front of the head's pages and the emptied pages go to the
+// pool's free list in (layer, b, h) order, where the next promotions take them from (:694-709).
+//
+// Numerics follow the reference's torch expressions: the q . k products accumulate in fp32 and are
+// rounded to bf16, the scaled score is rounded to bf16 again, the softmax is fp32.
+//
+// Kernels (per layer): row statistics (online max / sum over all keys, one CTA per 128 window
+// rows); key scores (one CTA per 64-key chunk, all window rows, mma.sync m16n8k16); select +
+// compact (one CTA per head).  After all layers: free-list append (one CTA).
+#include "common.cuh"
+
+namespace wgkv {
+namespace {
+
+constexpr int kSnThreads = 256;
+constexpr int kSnWarps = kSnThreads / 32;
+constexpr int kKeys = 64;                 // keys per shared-memory chunk
+constexpr int kRowsPerCta = 16 * kSnWarps;  // row statistics: one 16-row tile per warp
+
+struct SnapArgs {
+  wgkv_pool P;
+  const uint16_t* qbuf;  // (layers, batch, win, Hq, D)
+  int win, Hq, G, R;     // R = win * G rows per head
+  float scale;
+  int layer;
+  float2* rowml;   // [BH][R] (max, sum)
+  float* scores;   // [BH][max_tokens]
+  int max_tok;
+};
+
+// Q fragment rows r0 = tile*16 + g, r1 = r0 + 8 of head bh; row r = w * G + g_idx.
+WGKV_DEV const uint16_t* qrow(const SnapArgs& a, int b, int h, int r) {
+  const int w = r / a.G, gi = r - w * a.G;
+  return a.qbuf + ((int64_t(a.layer) * a.P.batch + b) * a.win + w) * int64_t(a.Hq) * a.P.head_dim +
+         int64_t(h * a.G + gi) * a.P.head_dim;
+}
+
+template <int D>
+WGKV_DEV void load_q_frag(const SnapArgs& a, int b, int h, int tile, uint32_t (&qa)[D / 16][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int r0 = tile * 16 + g, r1 = r0 + 8;
+  const uint32_t* q0 = reinterpret_cast<const uint32_t*>(qrow(a, b, h, r0));
+  const uint32_t* q1 = reinterpret_cast<const uint32_t*>(qrow(a, b, h, r1));
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int c = kk * 16 + 2 * t4;
+    qa[kk][0] = __ldg(q0 + c / 2);
+    qa[kk][1] = __ldg(q1 + c / 2);
+    qa[kk][2] = __ldg(q0 + (c + 8) / 2);
+    qa[kk][3] = __ldg(q1 + (c + 8) / 2);
+  }
+}
+
+// keys [k0, k0 + kKeys) of head bh into shared memory (rows padded to D + 8), zeros past glen
+template <int D>
+WGKV_DEV void load_keys(const wgkv_pool& P, const int32_t* grow, int k0, int glen, uint16_t* ks) {
+  constexpr int V = D / 8;  // 16-byte vectors per row
+  const int T = P.page;
+  for (int e = threadIdx.x; e < kKeys * V; e += kSnThreads) {
+    const int r = e / V, c = e - r * V, p = k0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (p < glen) {
+      const int64_t row = int64_t(grow[p / T]) * T + p % T;
+      v = *reinterpret_cast<const uint4*>(P.k + row * D + c * 8);
+    }
+    *reinterpret_cast<uint4*>(ks + r * (D + 8) + c * 8) = v;
+  }
+}
+
+// S tile (16 rows x 64 keys) of one warp, rounded as bf16(bf16(q . k) * scale)
+template <int D>
+WGKV_DEV void score_tile(const uint32_t (&qa)[D / 16][4], const uint16_t* ks, float scale, float (&s)[8][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(ks + (j * 8 + g) * (D + 8));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t b0 = kr[(kk * 16 + 2 * t4) / 2], b1 = kr[(kk * 16 + 8 + 2 * t4) / 2];
+      mma_bf16_16816(s[j], qa[kk], b0, b1);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[j][e] = bf16_round(bf16_round(s[j][e]) * scale);
+}
+
+// ---- row statistics: max and sum of exp over all of the head's keys, online ----
+template <int D>
+__global__ void __launch_bounds__(kSnThreads) snap_rowstats_kernel(SnapArgs a) {
+  extern __shared__ __align__(16) uint8_t sn_smem[];
+  uint16_t* ks = reinterpret_cast<uint16_t*>(sn_smem);
+  const wgkv_pool& P = a.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk;
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int glen = P.global_lengths[int64_t(a.layer) * BH + bh];
+  if (glen == 0) return;
+  const int32_t* grow = P.block_table + (int64_t(a.layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page;
+  const int tile = blockIdx.x * kSnWarps + warp;
+  const bool active = tile * 16 < a.R;
+  uint32_t qa[D / 16][4];
+  if (active) load_q_frag<D>(a, b, h, tile, qa);
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  for (int k0 = 0; k0 < glen; k0 += kKeys) {
+    __syncthreads();
+    load_keys<D>(P, grow, k0, glen, ks);
+    __syncthreads();
+    if (!active) continue;
+    float s[8][4];
+    score_tile<D>(qa, ks, a.scale, s);
+    float x0 = -INFINITY, x1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = k0 + j * 8 + 2 * t4;
+      if (c < glen) { x0 = fmaxf(x0, s[j][0]); x1 = fmaxf(x1, s[j][2]); }
+      if (c + 1 < glen) { x0 = fmaxf(x0, s[j][1]); x1 = fmaxf(x1, s[j][3]); }
+    }
+    for (int o = 1; o < 4; o <<= 1) {
+      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffff, x0, o));
+      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffff, x1, o));
+    }
+    const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+    float e0 = 0.f, e1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = k0 + j * 8 + 2 * t4;
+      if (c < glen) { e0 += expf(s[j][0] - n0); e1 += expf(s[j][2] - n1); }
+      if (c + 1 < glen) { e0 += expf(s[j][1] - n0); e1 += expf(s[j][3] - n1); }
+    }
+    for (int o = 1; o < 4; o <<= 1) {
+      e0 += __shfl_xor_sync(0xffffffff, e0, o);
+      e1 += __shfl_xor_sync(0xffffffff, e1, o);
+    }
+    l0 = l0 * expf(m0 - n0) + e0;  // expf(-inf) = 0 on the first chunk
+    l1 = l1 * expf(m1 - n1) + e1;
+    m0 = n0;
+    m1 = n1;
+  }
+  if (active && t4 == 0) {
+    const int r0 = tile * 16 + g;
+    a.rowml[int64_t(bh) * a.R + r0] = make_float2(m0, l0);
+    a.rowml[int64_t(bh) * a.R + r0 + 8] = make_float2(m1, l1);
+  }
+}
+
+// ---- key scores: softmax probability, max over the group, mean over the window ----
+template <int D>
+__global__ void __launch_bounds__(kSnThreads) snap_scores_kernel(SnapArgs a) {
+  extern __shared__ __align__(16) uint8_t sn_smem[];
+  uint16_t* ks = reinterpret_cast<uint16_t*>(sn_smem);
+  float* acc = reinterpret_cast<float*>(ks + kKeys * (D + 8));  // [kKeys]
+  const wgkv_pool& P = a.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk;
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int glen = P.global_lengths[int64_t(a.layer) * BH + bh];
+  const int k0 = blockIdx.x * kKeys;
+  if (k0 >= glen) return;
+  const int32_t* grow = P.block_table + (int64_t(a.layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page;
+  for (int i = threadIdx.x; i < kKeys; i += kSnThreads) acc[i] = 0.f;
+  load_keys<D>(P, grow, k0, glen, ks);
+  __syncthreads();
+  float col[8][2];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) col[j][0] = col[j][1] = 0.f;
+  const int G = a.G;
+  for (int tile = warp; tile * 16 < a.R; tile += kSnWarps) {
+    uint32_t qa[D / 16][4];
+    load_q_frag<D>(a, b, h, tile, qa);
+    float s[8][4];
+    score_tile<D>(qa, ks, a.scale, s);
+    const int r0 = tile * 16 + g, r1 = r0 + 8;
+    const float2 ml0 = a.rowml[int64_t(bh) * a.R + r0], ml1 = a.rowml[int64_t(bh) * a.R + r1];
+    const float inv0 = 1.f / ml0.y, inv1 = 1.f / ml1.y;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float p0 = expf(s[j][e] - ml0.x) * inv0;      // row r0
+        float p1 = expf(s[j][2 + e] - ml1.x) * inv1;  // row r1
+        // max over the G rows of a window position (rows w * G .. w * G + G - 1)
+        for (int o = 4; o < 4 * G && o < 32; o <<= 1) {
+          p0 = fmaxf(p0, __shfl_xor_sync(0xffffffff, p0, o));
+          p1 = fmaxf(p1, __shfl_xor_sync(0xffffffff, p1, o));
+        }
+        if (G == 16) p0 = p1 = fmaxf(p0, p1);
+        // one contribution per window position
+        col[j][e] += (r0 % G == 0 ? p0 : 0.f) + (r1 % G == 0 ? p1 : 0.f);
+      }
+    }
+  }
+  // sum over the lanes of a key column, then over warps
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float v = col[j][e];
+      for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+      if (g == 0) atomicAdd(&acc[j * 8 + 2 * t4 + e], v);
+    }
+  __syncthreads();
+  const float inv_win = 1.f / float(a.win);
+  for (int i = threadIdx.x; i < kKeys; i += kSnThreads)
+    if (k0 + i < glen) a.scores[int64_t(bh) * a.max_tok + k0 + i] = acc[i] * inv_win;
+}
+
+// ---- per head: max-pool, bottom-k, compaction ----
+WGKV_DEV uint32_t float_key(float f) {  // ascending float order -> ascending unsigned order
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+WGKV_DEV int block_scan_excl(int v, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffff, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int base = 0, tot = 0;
+  for (int w = 0; w < kSnWarps; ++w) {
+    if (w < warp) base += wsum[w];
+    tot += wsum[w];
+  }
+  __syncthreads();
+  *total = tot;
+  return base + x - v;
+}
+
+struct SelectArgs {
+  wgkv_pool P;
+  int layer, ks;
+  double ratio;
+  const float* scores;  // [BH][max_tok]
+  float* pooled;        // [BH][max_tok]
+  int max_tok;
+  int* nb;              // [layers][BH][2]: pages before / after
+};
+
+template <int D>
+__global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectArgs a) {
+  extern __shared__ __align__(16) uint8_t sn_smem[];
+  uint4* stage = reinterpret_cast<uint4*>(sn_smem);  // [kSnThreads][2 * D / 8]
+  const wgkv_pool& P = a.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk, T = P.page;
+  const int bh = blockIdx.x, tid = threadIdx.x;
+  __shared__ int hist[256];
+  __shared__ int wsum[kSnWarps];
+  __shared__ int s_bin, s_take;
+  int* gl = P.global_lengths + int64_t(a.layer) * BH + bh;
+  const int glen = *gl;
+  const int nb_old = (glen + T - 1) / T;
+  const int n_ev = int(double(glen) * a.ratio);
+  int* nb = a.nb + (int64_t(a.layer) * BH + bh) * 2;
+  if (n_ev == 0) {
+    if (tid == 0) { nb[0] = nb_old; nb[1] = nb_old; }
+    return;
+  }
+  const float* sc = a.scores + int64_t(bh) * a.max_tok;
+  float* pl = a.pooled + int64_t(bh) * a.max_tok;
+  const int pad = a.ks / 2;
+  for (int p = tid; p < glen; p += kSnThreads) {
+    float m = -INFINITY;
+    for (int d = -pad; d <= pad; ++d)
+      if (p + d >= 0 && p + d < glen) m = fmaxf(m, sc[p + d]);
+    pl[p] = m;
+  }
+  __syncthreads();
+  // n_ev-th smallest key, four 8-bit passes from the top byte
+  int need = n_ev;
+  uint32_t prefix = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += kSnThreads) hist[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < glen; p += kSnThreads) {
+      const uint32_t k = float_key(pl[p]);
+      if (pass == 0 || (k >> (shift + 8)) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0, bin = 0;
+      for (; bin < 255; ++bin) {
+        if (acc + hist[bin] >= need) break;
+        acc += hist[bin];
+      }
+      s_bin = bin;
+      s_take = need - acc;
+    }
+    __syncthreads();
+    prefix = (prefix << 8) | uint32_t(s_bin);
+    need = s_take;
+    __syncthreads();
+  }
+  const uint32_t kth = prefix;  // evict keys < kth and the first `need` equal to it
+  // in-place compaction, chunks of kSnThreads positions: read the kept rows, barrier, write
+  const int32_t* grow = P.block_table + (int64_t(a.layer) * BH + bh) * P.max_blocks_per_head + P.window / T;
+  constexpr int V = D / 8;
+  int eq_seen = 0, kept_base = 0;
+  for (int c0 = 0; c0 < glen; c0 += kSnThreads) {
+    const int p = c0 + tid;
+    uint32_t k = 0;
+    if (p < glen) k = float_key(pl[p]);
+    const int is_eq = p < glen && k == kth;
+    int tot_eq;
+    const int eq_rank = eq_seen + block_scan_excl(is_eq, wsum, &tot_eq);
+    const int keep = p < glen && !(k < kth || (is_eq && eq_rank < need));
+    int tot_keep;
+    const int dst = kept_base + block_scan_excl(keep, wsum, &tot_keep);
+    if (keep) {
+      const int64_t row = int64_t(grow[p / T]) * T + p % T;
+      const uint4* kr = reinterpret_cast<const uint4*>(P.k + row * D);
+      const uint4* vr = reinterpret_cast<const uint4*>(P.v + row * D);
+      for (int c = 0; c < V; ++c) {
+        stage[tid * 2 * V + c] = kr[c];
+        stage[tid * 2 * V + V + c] = vr[c];
+      }
+    }
+    __syncthreads();
+    if (keep && dst != p) {
+      const int64_t row = int64_t(grow[dst / T]) * T + dst % T;
+      uint4* kw = reinterpret_cast<uint4*>(P.k + row * D);
+      uint4* vw = reinterpret_cast<uint4*>(P.v + row * D);
+      for (int c = 0; c < V; ++c) {
+        kw[c] = stage[tid * 2 * V + c];
+        vw[c] = stage[tid * 2 * V + V + c];
+      }
+    }
+    __syncthreads();
+    eq_seen += tot_eq;
+    kept_base += tot_keep;
+  }
+  if (tid == 0) {
+    *gl = kept_base;
+    nb[0] = nb_old;
+    nb[1] = (kept_base + T - 1) / T;
+  }
+}
+
+// ---- freed pages -> the free list, (layer, b, h) order; their table entries -> sentinel ----
+constexpr int kFreeThreads = 1024;
+
+__global__ void __launch_bounds__(kFreeThreads) snap_free_kernel(wgkv_pool P, const int* nb) {
+  const int N = P.layers * P.batch * P.kv_heads;
+  const int per = (N + kFreeThreads - 1) / kFreeThreads;
+  const int i0 = min(N, int(threadIdx.x) * per), i1 = min(N, i0 + per);
+  int cnt = 0;
+  for (int i = i0; i < i1; ++i) cnt += nb[2 * i] - nb[2 * i + 1];
+  __shared__ int wsum[kFreeThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffff, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int base = 0, tot = 0;
+  for (int w = 0; w < kFreeThreads / 32; ++w) {
+    if (w < warp) base += wsum[w];
+    tot += wsum[w];
+  }
+  const int fc = *P.free_count;
+  int off = fc + base + x - cnt;
+  const int sentinel = int(P.total_blocks - 1);
+  for (int i = i0; i < i1; ++i) {
+    int32_t* row = P.block_table + int64_t(i) * P.max_blocks_per_head + P.window / P.page;
+    for (int j = nb[2 * i + 1]; j < nb[2 * i]; ++j) {
+      P.free_ids[off++] = row[j];
+      row[j] = sentinel;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *P.free_count = fc + tot;
+}
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace wgkv
+
+using namespace wgkv;
+
+extern "C" size_t wgkv_snapkv_workspace_size(const wgkv_pool* pool, int window, int q_heads) {
+  if (!pool || pool->kv_heads <= 0) return 0;
+  const size_t BH = size_t(pool->batch) * pool->kv_heads;
+  const size_t R = size_t(window) * (q_heads / pool->kv_heads);
+  return round256(BH * R * 8) + 2 * round256(BH * size_t(pool->max_tokens_per_head) * 4) +
+         round256(size_t(pool->layers) * BH * 8);
+}
+
+extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries, int window, int q_heads,
+                                 float softmax_scale, double evict_ratio, int kernel_size, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (!pool || !pool->free_ids || !pool->free_count || !queries || !workspace || window <= 0 || q_heads <= 0 ||
+      q_heads % pool->kv_heads || kernel_size <= 0 || kernel_size % 2 == 0 || !(evict_ratio > 0.0) ||
+      evict_ratio > 1.0)
+    return WGKV_EINVAL;
+  const int G = q_heads / pool->kv_heads, D = pool->head_dim;
+  if (16 % G || (window * G) % 16 || (D != 64 && D != 128)) return WGKV_EINVAL;
+  if (workspace_bytes < wgkv_snapkv_workspace_size(pool, window, q_heads)) return WGKV_ENOSPC;
+  const int BH = pool->batch * pool->kv_heads;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t R = size_t(window) * G;
+  SnapArgs a{};
+  a.P = *pool;
+  a.qbuf = queries;
+  a.win = window;
+  a.Hq = q_heads;
+  a.G = G;
+  a.R = int(R);
+  a.scale = softmax_scale;
+  a.rowml = reinterpret_cast<float2*>(ws);
+  a.scores = reinterpret_cast<float*>(ws + round256(size_t(BH) * R * 8));
+  a.max_tok = pool->max_tokens_per_head;
+  SelectArgs sa{};
+  sa.P = *pool;
+  sa.ks = kernel_size;
+  sa.ratio = evict_ratio;
+  sa.scores = a.scores;
+  sa.pooled = a.scores + round256(size_t(BH) * a.max_tok * 4) / 4;
+  sa.max_tok = a.max_tok;
+  sa.nb = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(sa.pooled) + round256(size_t(BH) * a.max_tok * 4));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t smem_keys = size_t(kKeys) * (D + 8) * 2;
+  const size_t smem_scores = smem_keys + kKeys * 4;
+  const size_t smem_stage = size_t(kSnThreads) * 2 * D * 2;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(snap_select_compact_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSnThreads * 2 * 64 * 2) != cudaSuccess ||
+        cudaFuncSetAttribute(snap_select_compact_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSnThreads * 2 * 128 * 2) != cudaSuccess)
+      return WGKV_ECUDA;
+    attr[dev] = true;
+  }
+  const int max_chunks = (pool->max_tokens_per_head + kKeys - 1) / kKeys;
+  for (int l = 0; l < pool->layers; ++l) {
+    a.layer = l;
+    sa.layer = l;
+    const dim3 g1((a.R + kRowsPerCta - 1) / kRowsPerCta, BH), g2(max_chunks, BH);
+    if (D == 128) {
+      snap_rowstats_kernel<128><<<g1, kSnThreads, smem_keys, s>>>(a);
+      snap_scores_kernel<128><<<g2, kSnThreads, smem_scores, s>>>(a);
+      snap_select_compact_kernel<128><<<BH, kSnThreads, smem_stage, s>>>(sa);
+    } else {
+      snap_rowstats_kernel<64><<<g1, kSnThreads, smem_keys, s>>>(a);
+      snap_scores_kernel<64><<<g2, kSnThreads, smem_scores, s>>>(a);
+      snap_select_compact_kernel<64><<<BH, kSnThreads, smem_stage, s>>>(sa);
+    }
+  }
+  snap_free_kernel<<<1, kFreeThreads, 0, s>>>(*pool, sa.nb);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}

@@ -22,6 +22,8 @@ from .layers import (  # noqa: F401
     refresh_local_is_global,
     self_attn_forward_patch,
     self_attn_decode_fused,
+    snapkv_evict,
+    snapkv_record_queries,
     self_attn_forward_patch_inference,
 )
 from .pool import RING_ON_DEVICE, WgkvPool, advance_host_ring, init_pool, ring_to_device  # noqa: F401

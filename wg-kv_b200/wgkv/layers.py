@@ -41,7 +41,9 @@ def _maybe_init(self, past_key_value, batch_size, key_states):
                   head_dim=self.head_dim, window=c.local_window_size, page=c.block_size,
                   max_total_tokens=c.max_total_tokens, max_tokens_per_head=c.max_tokens_per_head,
                   device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)),
-                  quest=bool(getattr(c, "use_quest", False)))
+                  quest=bool(getattr(c, "use_quest", False)),
+                  snapkv_window=c.snapkv_window_size if getattr(c, "snapkv_enabled", False) else None,
+                  q_heads=c.num_attention_heads)
     elif self.layer_idx == 0:
         raise AssertionError("prefill on an initialised cache (the reference asserts the same, :1197)")
 
@@ -214,10 +216,13 @@ def self_attn_forward_patch_inference(self, past_key_value, input_shape, query_s
     if (not is_prefilling) and self.layer_idx == 0 and _promote_now(past_key_value, c.local_window_size):
         migrate_local_kv_to_global(self, past_key_value, device, local_blocks_per_head)
     if is_prefilling:
-        return self.prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states,
-                                    batch_size, q_seq_len, device, g_mask, local_blocks_per_head)
-    return self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, g_mask,
-                               local_blocks_per_head)
+        out = self.prefill_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states,
+                                   batch_size, q_seq_len, device, g_mask, local_blocks_per_head)
+    else:
+        out = self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device,
+                                  g_mask, local_blocks_per_head)
+    _snapkv_after(self, past_key_value, query_states)
+    return out
 
 
 def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, input_shape, query_states, pre_key,
@@ -264,6 +269,7 @@ def self_attn_forward_patch(self, gating_mode, attention_mask, past_key_value, i
                                           c.g_threshold)
     out = self.decode_wrapper(self, past_key_value, query_states, pre_key, key_states, value_states, device, None,
                               local_blocks_per_head, appended=True)
+    _snapkv_after(self, past_key_value, query_states)
     return out, None, None
 
 
@@ -298,3 +304,53 @@ def self_attn_decode_fused(self, past_key_value, qkv, q_heads, position, rope_co
                                       gate=not defer)
     return self.decode_wrapper(self, past_key_value, q.view(B, q_heads, 1, self.head_dim), None, None, None,
                                device, None, W // c.block_size, appended=True)
+
+
+def snapkv_record_queries(self, past_key_value, query_states):
+    """:579-592 with a batch axis: keep the last ``snapkv_window_size`` queries of every layer
+    (post-RoPE, (B, Hq, L, D)) in ``snapkv_query_buffer``; length / pointer advance at the last layer."""
+    c = _cfg(self)
+    win = c.snapkv_window_size
+    buf = past_key_value.snapkv_query_buffer[self.layer_idx]  # (B, win, Hq, D)
+    L = query_states.shape[2]
+    if L > 1:
+        take = min(win, L)
+        buf[:, :take].copy_(query_states[:, :, L - take:].transpose(1, 2))
+        if self.layer_idx == c.num_hidden_layers - 1:
+            past_key_value.snapkv_query_length = take
+            past_key_value.snapkv_query_ptr = take % win
+    else:
+        buf[:, past_key_value.snapkv_query_ptr].copy_(query_states[:, :, 0])
+        if self.layer_idx == c.num_hidden_layers - 1:
+            past_key_value.snapkv_query_length = min(win, past_key_value.snapkv_query_length + 1)
+            past_key_value.snapkv_query_ptr = (past_key_value.snapkv_query_ptr + 1) % win
+
+
+def snapkv_evict(self, past_key_value, device, local_blocks_per_head):
+    """:595-671 for every layer and head at once (``wgkv_snapkv_evict``)."""
+    c = _cfg(self)
+    assert past_key_value.snapkv_query_length == c.snapkv_window_size
+    nbytes = int(lib.wgkv_snapkv_workspace_size(pool_ref(past_key_value), c.snapkv_window_size,
+                                                c.num_attention_heads))
+    ws = workspace(device, "snapkv", nbytes)
+    st = lib.wgkv_snapkv_evict(pool_ref(past_key_value), past_key_value.snapkv_query_buffer.data_ptr(),
+                               c.snapkv_window_size, c.num_attention_heads, float(self.scaling),
+                               float(c.snapkv_evict_ratio), int(c.snapkv_kernel_size), ws.data_ptr(), ws.numel(),
+                               stream_ptr(device))
+    check(st, "wgkv_snapkv_evict")
+
+
+def _snapkv_after(self, past_key_value, query_states):
+    """The SnapKV hook that follows the attention of every layer (:1500-1507): record the queries,
+    and after the last layer evict when the global tokens exceed snapkv_max_cached_tokens (one host
+    read of the total, as in the reference)."""
+    c = _cfg(self)
+    if not getattr(c, "snapkv_enabled", False):
+        return
+    if _device_ring(past_key_value):
+        raise NotImplementedError("SnapKV decides on the host; it is not captured in decode graphs")
+    snapkv_record_queries(self, past_key_value, query_states)
+    if self.layer_idx == c.num_hidden_layers - 1 and \
+            int(past_key_value.global_lengths.sum().item()) > c.snapkv_max_cached_tokens:
+        past_key_value.snapkv_evict_count += 1
+        snapkv_evict(self, past_key_value, query_states.device, c.local_window_size // c.block_size)

@@ -41,11 +41,13 @@ class WgkvPool(ctypes.Structure):
         ("ring_state", ctypes.c_void_p),
         ("quest_min", ctypes.c_void_p),
         ("quest_max", ctypes.c_void_p),
+        ("free_ids", ctypes.c_void_p),
+        ("free_count", ctypes.c_void_p),
     ]
 
 
 def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_total_tokens, max_tokens_per_head,
-              device, dtype=torch.bfloat16, defer=False, quest=False):
+              device, dtype=torch.bfloat16, defer=False, quest=False, snapkv_window=None, q_heads=None):
     """Allocate the pool on ``cache`` (any attribute holder), as prefill_wrapper does at layer 0."""
     assert window % page == 0, "local_window_size must be a multiple of block_size"
     local_pages = window // page
@@ -77,6 +79,14 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     # device copy of (local_length, local_ptr), used when a decode step runs as a CUDA graph
     cache.ring_state = torch.zeros(2, dtype=torch.int32, device=dev)
     cache.wgkv_device_ring = False
+    if snapkv_window:  # SnapKV state (modeling_layers.py:1249-1262), a batch axis on the query window
+        cache.snapkv_query_buffer = torch.zeros(layers, batch, snapkv_window, q_heads, head_dim, dtype=dtype,
+                                                device=dev)
+        cache.snapkv_query_length = 0
+        cache.snapkv_query_ptr = 0
+        cache.snapkv_evict_count = 0
+        cache.free_block_ids = torch.zeros(total_blocks, dtype=torch.int32, device=dev)
+        cache.free_block_count = torch.zeros(1, dtype=torch.int32, device=dev)
     if quest:  # per-page key bounds for QUEST selection (modeling_layers.py:1232-1240)
         cache.quest_block_key_min = torch.zeros(total_blocks, head_dim, dtype=dtype, device=dev)
         cache.quest_block_key_max = torch.zeros(total_blocks, head_dim, dtype=dtype, device=dev)
@@ -96,6 +106,8 @@ def init_pool(cache, *, layers, batch, kv_heads, head_dim, window, page, max_tot
     s.ring_state = cache.ring_state.data_ptr()
     s.quest_min = cache.quest_block_key_min.data_ptr() if quest else None
     s.quest_max = cache.quest_block_key_max.data_ptr() if quest else None
+    s.free_ids = cache.free_block_ids.data_ptr() if snapkv_window else None
+    s.free_count = cache.free_block_count.data_ptr() if snapkv_window else None
     cache.wgkv_pool = s
     cache.gated_kv_initialized = True
     return cache
