@@ -43,7 +43,7 @@ def _maybe_init(self, past_key_value, batch_size, key_states):
                   device=key_states.device, dtype=key_states.dtype, defer=bool(getattr(c, "g_defer", False)),
                   quest=bool(getattr(c, "use_quest", False)),
                   snapkv_window=c.snapkv_window_size if getattr(c, "snapkv_enabled", False) else None,
-                  q_heads=c.num_attention_heads)
+                  q_heads=getattr(c, "num_attention_heads", None))
     elif self.layer_idx == 0:
         raise AssertionError("prefill on an initialised cache (the reference asserts the same, :1197)")
 
