@@ -277,6 +277,15 @@ WGKV_API int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows,
  * weight), fp32 accumulation, y bf16 (or fp32 when out_f32, then without residual) rows y_stride
  * apart.  residual may alias y (in-place y += x w^T).  k % 8 == 0, 16-byte aligned x and w.
  */
+/*
+ * out[r * out_stride] = argmax_j logits[r, j] (int64; the first index among equal maxima, as
+ * torch.argmax) for rows <= 65535 fp32 rows of n entries.  workspace of
+ * wgkv_argmax_workspace_size(rows, n) bytes whose first `rows` ints are zero before the first call
+ * (the kernel leaves them zero).
+ */
+WGKV_API size_t wgkv_argmax_workspace_size(int rows, int n);
+WGKV_API int wgkv_argmax(const float* logits, int64_t row_stride, int rows, int n, int64_t* out, int64_t out_stride,
+                         void* workspace, size_t workspace_bytes, void* stream);
 WGKV_API int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
                               int64_t y_stride, int out_f32, const uint16_t* residual, int64_t r_stride,
                               void* stream);

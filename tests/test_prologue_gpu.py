@@ -169,3 +169,15 @@ def test_skinny_gemm_matches_fp32(m, n, k):
     r0 = r.float().clone()
     skinny_linear(x, w, residual=r)  # in place
     torch.testing.assert_close(r.float(), r0 + ref, **tol)
+
+
+@pytest.mark.parametrize("rows,n", [(1, 128256), (3, 151936), (8, 100), (2, 4096)])
+def test_argmax_matches_torch(rows, n):
+    from wgkv.model import argmax_into
+    x = torch.randn(rows, n, device="cuda")
+    x[0, n // 3] = 50.0
+    x[0, n // 2] = 50.0  # a tie: the first index wins, as torch.argmax
+    out = torch.empty(rows, 1, dtype=torch.int64, device="cuda")
+    for _ in range(3):  # the ticket counters reset themselves between calls
+        argmax_into(x, out)
+        assert torch.equal(out, x.argmax(-1, keepdim=True))

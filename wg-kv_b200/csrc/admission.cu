@@ -573,13 +573,14 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
     const float sn = tid < D ? bf2f(R.sin[pos * D + tid]) : 0.f;
     const uint16_t* qkv = R.qkv + b * R.sb;
     const int G = R.Hq / Hk;
-    if (tid < D) stage[2][tid] = qkv[int64_t(R.Hq + Hk + h) * D + tid];
-    norm_rope_row(qkv + int64_t(R.Hq + h) * D, R.k_norm, R.eps, c, sn, D, xs, part, stage[0], stage[1]);
-    for (int q = 0; q < G; ++q) {
-      const int hq = h * G + q;
+    if (blockIdx.y > 0) {  // CTAs 1..G of the head: one query row each
+      const int hq = h * G + blockIdx.y - 1;
       norm_rope_row(qkv + int64_t(hq) * D, R.q_norm, R.eps, c, sn, D, xs, part, nullptr,
                     R.q_out + (int64_t(b) * R.Hq + hq) * D);
+      return;
     }
+    if (tid < D) stage[2][tid] = qkv[int64_t(R.Hq + Hk + h) * D + tid];
+    norm_rope_row(qkv + int64_t(R.Hq + h) * D, R.k_norm, R.eps, c, sn, D, xs, part, stage[0], stage[1]);
     k_src = stage[1];
     v_src = stage[2];
     if (!g.w1 && P.local_pre_key) copy_row<false>(P.local_pre_key + row * D, stage[0], D, tid, kDgaThreads);
@@ -896,7 +897,8 @@ extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert
   }
   PoolArgs pa{*pool};
   const int BH = pool->batch * pool->kv_heads;
-  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, R, layer, insert_pos, cur_local_len,
-                                                                       RowSrc{}, RowSrc{}, cache_seqlens);
+  // one CTA per (b, h) for the key, gate and append, plus one per query head of the group
+  decode_gate_append_kernel<<<dim3(BH, 1 + q_heads / pool->kv_heads), kDgaThreads, 0, as_stream(stream)>>>(
+      pa, g, R, layer, insert_pos, cur_local_len, RowSrc{}, RowSrc{}, cache_seqlens);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

@@ -207,6 +207,53 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_rows_kernel(const uint16
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// greedy token: argmax of each fp32 logits row (first index on ties, as torch.argmax); one launch,
+// chunk partials per CTA, the last CTA of a row (atomic ticket, reset for the next call) finishes.
+constexpr int kAmThreads = 256;
+constexpr int kAmChunk = 4096;
+
+WGKV_DEV void am_better(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
+}
+
+__global__ void __launch_bounds__(kAmThreads) argmax_kernel(const float* x, int64_t xs, int n, float* pv, int* pi,
+                                                           int* ticket, int64_t* out, int64_t os) {
+  const int r = blockIdx.y, c = blockIdx.x, nc = gridDim.x, tid = threadIdx.x;
+  const float* row = x + int64_t(r) * xs;
+  float v = -INFINITY;
+  int i = 0x7fffffff;
+  for (int j = c * kAmChunk + tid; j < min(n, (c + 1) * kAmChunk); j += kAmThreads) am_better(v, i, row[j], j);
+  for (int o = 16; o; o >>= 1) am_better(v, i, __shfl_xor_sync(0xffffffff, v, o), __shfl_xor_sync(0xffffffff, i, o));
+  __shared__ float sv[kAmThreads / 32];
+  __shared__ int si[kAmThreads / 32];
+  __shared__ int s_last;
+  if ((tid & 31) == 0) { sv[tid >> 5] = v; si[tid >> 5] = i; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kAmThreads / 32; ++w) am_better(v, i, sv[w], si[w]);
+    pv[int64_t(r) * nc + c] = v;
+    pi[int64_t(r) * nc + c] = i;
+    __threadfence();
+    const int t = atomicAdd(&ticket[r], 1);
+    s_last = t == nc - 1;
+    if (s_last) ticket[r] = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  v = -INFINITY;
+  i = 0x7fffffff;
+  for (int k = tid; k < nc; k += kAmThreads) am_better(v, i, __ldcg(pv + int64_t(r) * nc + k), __ldcg(pi + int64_t(r) * nc + k));
+  for (int o = 16; o; o >>= 1) am_better(v, i, __shfl_xor_sync(0xffffffff, v, o), __shfl_xor_sync(0xffffffff, i, o));
+  if ((tid & 31) == 0) { sv[tid >> 5] = v; si[tid >> 5] = i; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kAmThreads / 32; ++w) am_better(v, i, sv[w], si[w]);
+    out[int64_t(r) * os] = i;
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -269,5 +316,23 @@ extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, cons
     default: WGKV_SG(8); break;
   }
 #undef WGKV_SG
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+extern "C" size_t wgkv_argmax_workspace_size(int rows, int n) {
+  const size_t nc = (size_t(n) + kAmChunk - 1) / kAmChunk;
+  return size_t(rows) * (nc * 8 + 4) + 256;
+}
+
+extern "C" int wgkv_argmax(const float* logits, int64_t row_stride, int rows, int n, int64_t* out, int64_t out_stride,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (!logits || !out || !workspace || rows <= 0 || n <= 0 || rows > 65535) return WGKV_EINVAL;
+  if (workspace_bytes < wgkv_argmax_workspace_size(rows, n)) return WGKV_ENOSPC;
+  const int nc = (n + kAmChunk - 1) / kAmChunk;
+  int* ticket = static_cast<int*>(workspace);  // rows ints, zero before the first call, left zero
+  float* pv = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t(rows) * 4 + 255) & ~size_t(255)));
+  int* pi = reinterpret_cast<int*>(pv + size_t(rows) * nc);
+  argmax_kernel<<<dim3(nc, rows), kAmThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, row_stride, n, pv, pi,
+                                                                                      ticket, out, out_stride);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

@@ -97,6 +97,18 @@ def skinny_linear(x, w, residual=None, out_f32=False):
     return y
 
 
+def argmax_into(logits, out):
+    """``wgkv_argmax``: out (rows, 1) int64 = first index of each fp32 row's maximum."""
+    from .runtime import workspace
+    rows, n = logits.shape
+    assert logits.stride(1) == 1 and logits.dtype == torch.float32
+    nbytes = int(lib.wgkv_argmax_workspace_size(rows, n))
+    ws = workspace(logits.device, "argmax", nbytes, zero_prefix=((rows * 4 + 255) // 256) * 256)
+    check(lib.wgkv_argmax(logits.data_ptr(), logits.stride(0), rows, n, out.data_ptr(), out.stride(0), ws.data_ptr(),
+                          ws.numel(), stream_ptr(logits.device)), "wgkv_argmax")
+    return out
+
+
 def _rotate_half(x):
     h = x.shape[-1] // 2
     return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
@@ -331,7 +343,10 @@ class WgkvDecoder:
             c = cos.index_select(0, self.pos)
             n = sin.index_select(0, self.pos)
         logits = self.forward(self.token, cache, c, n)
-        self.token.copy_(logits.argmax(-1, keepdim=True))
+        if self.fused:
+            argmax_into(logits, self.token)
+        else:
+            self.token.copy_(logits.argmax(-1, keepdim=True))
         self.pos.add_(1)
         self.logits = logits
         return logits
