@@ -554,9 +554,11 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
   const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim;
   const int i = blockIdx.x, b = i / Hk, h = i - b * Hk;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // launched early behind the previous kernel (programmatic dependent launch): wait for its results
+  griddep_wait();
   ring_position(P, ins, cur);
   // the paged-decode launch that follows may start its set-up now (it waits for this grid's results)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  griddep_launch();
   __shared__ float xs[384];
   __shared__ float part[kDgaThreads / 32];
   __shared__ __align__(16) uint16_t stage[3][128];
@@ -846,9 +848,10 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
   PoolArgs pa{*pool};
   RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0};
   const int BH = pool->batch * pool->kv_heads;
-  decode_gate_append_kernel<<<BH, kDgaThreads, 0, as_stream(stream)>>>(pa, g, RopeParams{}, layer, insert_pos,
-                                                                       cur_local_len, K, V, cache_seqlens);
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  if (launch_pdl(decode_gate_append_kernel, dim3(BH), dim3(kDgaThreads), 0, as_stream(stream), pa, g, RopeParams{},
+                 layer, insert_pos, cur_local_len, K, V, cache_seqlens) != cudaSuccess)
+    return WGKV_ECUDA;
+  return WGKV_OK;
 }
 
 extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_pos, int cur_local_len,
@@ -898,7 +901,9 @@ extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert
   PoolArgs pa{*pool};
   const int BH = pool->batch * pool->kv_heads;
   // one CTA per (b, h) for the key, gate and append, plus one per query head of the group
-  decode_gate_append_kernel<<<dim3(BH, 1 + q_heads / pool->kv_heads), kDgaThreads, 0, as_stream(stream)>>>(
-      pa, g, R, layer, insert_pos, cur_local_len, RowSrc{}, RowSrc{}, cache_seqlens);
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  if (launch_pdl(decode_gate_append_kernel, dim3(BH, 1 + q_heads / pool->kv_heads), dim3(kDgaThreads), 0,
+                 as_stream(stream), pa, g, R, layer, insert_pos, cur_local_len, RowSrc{}, RowSrc{},
+                 cache_seqlens) != cudaSuccess)
+    return WGKV_ECUDA;
+  return WGKV_OK;
 }

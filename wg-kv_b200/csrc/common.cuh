@@ -129,6 +129,28 @@ WGKV_DEV uint16_t f2bf(float x) { return __bfloat16_as_ushort(__float2bfloat16_r
 // 1024-byte aligned): the chunk index is XORed with row % 8.
 WGKV_DEV uint32_t swz128(uint32_t row, uint32_t chunk) { return row * 128u + ((chunk ^ (row & 7u)) << 4); }
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may start while the previous
+// kernel of the stream finishes; it must call griddep_wait() before touching anything that kernel
+// writes (or reads and it overwrites).  griddep_launch() lets the next kernel start early.
+WGKV_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+WGKV_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 WGKV_DEV void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }

@@ -38,6 +38,8 @@ constexpr int kMaxVec = 4;
 __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* x, int64_t xs, const uint16_t* w,
                                                                int cols, float eps, uint16_t* out, int64_t os) {
   const int r = blockIdx.x, tid = threadIdx.x;
+  griddep_launch();
+  griddep_wait();
   const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(r) * xs);
   const int nv = cols / 8;
   float v[kMaxVec][8];
@@ -78,6 +80,8 @@ __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* x
 __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const uint16_t* gu, int64_t gs, int rows,
                                                                int inter, uint16_t* out, int64_t os) {
   const int c = blockIdx.x * kRowThreads + threadIdx.x;
+  griddep_launch();
+  griddep_wait();
   if (c >= inter / 8) return;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const uint4* g4 = reinterpret_cast<const uint4*>(gu + r * gs);
@@ -112,13 +116,23 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16
   float acc[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) acc[m] = 0.f;
-  if (row < n) {
-    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(row) * k);
-    for (int cb = c0 + lane; cb < c1; cb += 32 * kSgUnroll) {
-      uint4 wv[kSgUnroll];
+  griddep_launch();
+  const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(min(row, n - 1)) * k);
+  // the first pass of weight loads does not depend on the previous kernel: issue it before waiting
+  uint4 wv[kSgUnroll];
 #pragma unroll
-      for (int u = 0; u < kSgUnroll; ++u)
-        wv[u] = cb + 32 * u < c1 ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);  // streamed once
+  for (int u = 0; u < kSgUnroll; ++u) {
+    const int c = c0 + lane + 32 * u;
+    wv[u] = row < n && c < c1 ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
+  }
+  griddep_wait();
+  if (row < n) {
+    for (int cb = c0 + lane; cb < c1; cb += 32 * kSgUnroll) {
+      if (cb != c0 + lane) {
+#pragma unroll
+        for (int u = 0; u < kSgUnroll; ++u)
+          wv[u] = cb + 32 * u < c1 ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);  // streamed once
+      }
 #pragma unroll
       for (int u = 0; u < kSgUnroll; ++u) {
         const int c = cb + 32 * u;
@@ -169,16 +183,28 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_rows_kernel(const uint16
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kSgWarps + (threadIdx.x >> 5), nw = gridDim.x * kSgWarps;
   const int kc = k / 8;
+  griddep_launch();
+  uint4 wv[kSgUnroll];
+  {  // the first row's first pass of weight loads goes out before waiting for the previous kernel
+    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(min(gw, n - 1)) * k);
+#pragma unroll
+    for (int u = 0; u < kSgUnroll; ++u) {
+      const int c = lane + 32 * u;
+      wv[u] = gw < n && c < kc ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  griddep_wait();
   for (int row = gw; row < n; row += nw) {
     const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(row) * k);
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0.f;
     for (int cb = lane; cb < kc; cb += 32 * kSgUnroll) {
-      uint4 wv[kSgUnroll];
+      if (row != gw || cb != lane) {
 #pragma unroll
-      for (int u = 0; u < kSgUnroll; ++u)
-        wv[u] = cb + 32 * u < kc ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < kSgUnroll; ++u)
+          wv[u] = cb + 32 * u < kc ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
       for (int u = 0; u < kSgUnroll; ++u) {
         const int c = cb + 32 * u;
@@ -220,6 +246,8 @@ WGKV_DEV void am_better(float& v, int& i, float v2, int i2) {
 __global__ void __launch_bounds__(kAmThreads) argmax_kernel(const float* x, int64_t xs, int n, float* pv, int* pi,
                                                            int* ticket, int64_t* out, int64_t os) {
   const int r = blockIdx.y, c = blockIdx.x, nc = gridDim.x, tid = threadIdx.x;
+  griddep_launch();
+  griddep_wait();
   const float* row = x + int64_t(r) * xs;
   float v = -INFINITY;
   int i = 0x7fffffff;
@@ -267,9 +295,10 @@ extern "C" int wgkv_rms_norm(const uint16_t* x, int64_t x_stride, const uint16_t
       x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(weight) || !aligned16(out))
     return WGKV_EINVAL;
   if (rows == 0) return WGKV_OK;
-  rms_norm_kernel<<<rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, x_stride, weight, cols, eps, out,
-                                                                                out_stride);
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  if (launch_pdl(rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), x, x_stride,
+                 weight, cols, eps, out, out_stride) != cudaSuccess)
+    return WGKV_ECUDA;
+  return WGKV_OK;
 }
 
 extern "C" int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows, int inter, uint16_t* out,
@@ -279,9 +308,10 @@ extern "C" int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int row
     return WGKV_EINVAL;
   if (rows == 0) return WGKV_OK;
   dim3 grid((inter / 8 + kRowThreads - 1) / kRowThreads, rows < 65535 ? rows : 65535);
-  silu_mul_kernel<<<grid, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(gate_up, gu_stride, rows, inter, out,
-                                                                                out_stride);
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  if (launch_pdl(silu_mul_kernel, grid, dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), gate_up, gu_stride,
+                 rows, inter, out, out_stride) != cudaSuccess)
+    return WGKV_ECUDA;
+  return WGKV_OK;
 }
 
 extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
@@ -298,13 +328,12 @@ extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, cons
   const bool rows = rpb == kSgWarps && int64_t(n) >= int64_t(kSgWarps) * 8 * sms;
   const int blocks = rows ? 8 * sms : (n + rpb - 1) / rpb;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
 #define WGKV_SG(MM)                                                                                            \
-  if (rows)                                                                                                    \
-    skinny_rows_kernel<MM><<<blocks, kSgWarps * 32, 0, s>>>(x, x_stride, w, n, k, y, y_stride, out_f32,        \
-                                                            residual, r_stride);                              \
-  else                                                                                                         \
-    skinny_gemm_kernel<MM><<<blocks, kSgWarps * 32, 0, s>>>(x, x_stride, w, n, k, rpb, y, y_stride, out_f32,   \
-                                                            residual, r_stride)
+  e = rows ? launch_pdl(skinny_rows_kernel<MM>, dim3(blocks), dim3(kSgWarps * 32), 0, s, x, x_stride, w, n, k, y,  \
+                        y_stride, out_f32, residual, r_stride)                                                 \
+           : launch_pdl(skinny_gemm_kernel<MM>, dim3(blocks), dim3(kSgWarps * 32), 0, s, x, x_stride, w, n, k,     \
+                        rpb, y, y_stride, out_f32, residual, r_stride)
   switch (m) {
     case 1: WGKV_SG(1); break;
     case 2: WGKV_SG(2); break;
@@ -316,7 +345,7 @@ extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, cons
     default: WGKV_SG(8); break;
   }
 #undef WGKV_SG
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  return e == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
 extern "C" size_t wgkv_argmax_workspace_size(int rows, int n) {
@@ -332,7 +361,8 @@ extern "C" int wgkv_argmax(const float* logits, int64_t row_stride, int rows, in
   int* ticket = static_cast<int*>(workspace);  // rows ints, zero before the first call, left zero
   float* pv = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t(rows) * 4 + 255) & ~size_t(255)));
   int* pi = reinterpret_cast<int*>(pv + size_t(rows) * nc);
-  argmax_kernel<<<dim3(nc, rows), kAmThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, row_stride, n, pv, pi,
-                                                                                      ticket, out, out_stride);
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  if (launch_pdl(argmax_kernel, dim3(nc, rows), dim3(kAmThreads), 0, static_cast<cudaStream_t>(stream), logits,
+                 row_stride, n, pv, pi, ticket, out, out_stride) != cudaSuccess)
+    return WGKV_ECUDA;
+  return WGKV_OK;
 }

@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmV);
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  griddep_launch();  // the next kernel (e.g. the output projection) may start fetching its weights
 
   // ---- prefix sum of 16-token units per (b, h) ---------------------------
   {
