@@ -272,12 +272,6 @@ WGKV_API int wgkv_rms_norm(const uint16_t* x, int64_t x_stride, const uint16_t* 
 WGKV_API int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows, int inter, uint16_t* out,
                            int64_t out_stride, void* stream);
 /*
- * y[i, j] = sum_k x[i, k] * w[j, k] (+ residual[i, j]) for the few rows of a decode step
- * (1 <= m <= 8): x (m, k) bf16 rows x_stride apart, w (n, k) bf16 row-major (a torch Linear
- * weight), fp32 accumulation, y bf16 (or fp32 when out_f32, then without residual) rows y_stride
- * apart.  residual may alias y (in-place y += x w^T).  k % 8 == 0, 16-byte aligned x and w.
- */
-/*
  * out[r * out_stride] = argmax_j logits[r, j] (int64; the first index among equal maxima, as
  * torch.argmax) for rows <= 65535 fp32 rows of n entries.  workspace of
  * wgkv_argmax_workspace_size(rows, n) bytes whose first `rows` ints are zero before the first call
@@ -286,9 +280,19 @@ WGKV_API int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int rows,
 WGKV_API size_t wgkv_argmax_workspace_size(int rows, int n);
 WGKV_API int wgkv_argmax(const float* logits, int64_t row_stride, int rows, int n, int64_t* out, int64_t out_stride,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * y[i, j] = sum_k x[i, k] * w[j, k] (+ residual[i, j]) for the few rows of a decode step
+ * (1 <= m <= 8): x (m, k) bf16 rows x_stride apart, w (n, k) bf16 row-major (a torch Linear
+ * weight), fp32 accumulation, y bf16 (or fp32 when out_f32, then without residual) rows y_stride
+ * apart.  residual may alias y (in-place y += x w^T).  k % 8 == 0, 16-byte aligned x and w.
+ * rms_weight != NULL: x is RMS-normalised first, exactly as wgkv_rms_norm would (k weights, eps).
+ * paired: w = [gate (n/2 rows) | up (n/2 rows)] and y (m, n/2) = silu(x gate^T) * (x up^T) with the
+ * roundings of wgkv_silu_mul on the bf16 projections (no residual, bf16 out).
+ */
 WGKV_API int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
                               int64_t y_stride, int out_f32, const uint16_t* residual, int64_t r_stride,
-                              void* stream);
+                              const uint16_t* rms_weight, float rms_eps, int paired, void* stream);
 
 /* ---- (a9-a11) vertical-slash sparse indices -------------------------------- */
 /*

@@ -27,3 +27,25 @@ def test_version_without_gpu():
         pytest.skip("libwgkv.so not built")
     from wgkv import lib
     assert lib.wgkv_version() >= 1
+
+
+def test_every_entry_point_the_host_layer_calls_is_declared_and_exported():
+    """A function the Python layer calls but the header does not declare would be built with hidden
+    visibility (the library compiles with -fvisibility=hidden) and fail only on a GPU box."""
+    import ctypes
+    import glob
+    import os
+    import re
+    from wgkv._lib import LIB_PATH, parse_header
+    pkg = os.path.dirname(LIB_PATH)
+    repo = os.path.dirname(os.path.dirname(pkg))
+    used = set()
+    for f in (glob.glob(os.path.join(pkg, "*.py")) + glob.glob(os.path.join(repo, "tests", "*.py")) +
+              [os.path.join(repo, "bench.py"), os.path.join(repo, "__graft_entry__.py")]):
+        used |= set(re.findall(r"lib\.(wgkv_\w+)", open(f).read()))
+    declared = parse_header()
+    assert used, "no entry points found"
+    assert not (used - set(declared)), sorted(used - set(declared))
+    lib = ctypes.CDLL(LIB_PATH)
+    missing = [n for n in used if not hasattr(lib, n)]
+    assert not missing, missing

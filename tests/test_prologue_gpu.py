@@ -181,3 +181,25 @@ def test_argmax_matches_torch(rows, n):
     for _ in range(3):  # the ticket counters reset themselves between calls
         argmax_into(x, out)
         assert torch.equal(out, x.argmax(-1, keepdim=True))
+
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 2048, 2048), (2, 16384, 2048), (3, 3072, 4096)])
+def test_skinny_gemm_fused_norm_and_activation(m, n, k):
+    """rms_weight / paired reproduce rms_norm -> GEMM and GEMM -> silu_mul (same roundings)."""
+    from wgkv.model import rms_norm, silu_mul, skinny_linear
+    x = (torch.randn(m, k, device="cuda") * 2).to(torch.bfloat16)
+    nw = (torch.rand(k, device="cuda") + 0.5).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda") * 0.05).to(torch.bfloat16)
+    ref = skinny_linear(rms_norm(x, nw, 1e-5), w)
+    got = skinny_linear(x, w, rms_weight=nw, rms_eps=1e-5)
+    # the mean square may differ in its last bit (summation order): compare within bf16 rounding
+    torch.testing.assert_close(got.float(), ref.float(), atol=1e-2, rtol=1e-2)
+    assert (got == ref).float().mean().item() > 0.95
+    ref2 = silu_mul(skinny_linear(x, w))
+    got2 = skinny_linear(x, w, paired=True)
+    # same roundings; the projection's fp32 sum may take another order (K split across warps)
+    torch.testing.assert_close(got2.float(), ref2.float(), atol=1e-2, rtol=1e-2)
+    assert (got2 == ref2).float().mean().item() > 0.95
+    got3 = skinny_linear(x, w, paired=True, rms_weight=nw, rms_eps=1e-5)
+    torch.testing.assert_close(got3.float(), silu_mul(ref).float(), atol=2e-2, rtol=2e-2)

@@ -101,11 +101,85 @@ __global__ void __launch_bounds__(kRowThreads) silu_mul_kernel(const uint16_t* g
 constexpr int kSgWarps = 8;
 constexpr int kSgUnroll = 8;
 
+// x rows as the GEMM sees them: plain, or RMS-normalised on the fly (norm_w != NULL) with the
+// roundings of rms_norm_kernel, bf16(bf16(x * inv) * w)
+template <int M>
+struct XRows {
+  const uint16_t* x;
+  int64_t xs;
+  const uint16_t* norm_w;
+  const float* inv;  // [M] in shared memory when norm_w is set
+
+  WGKV_DEV void load(int m, int c, float* xf) const {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), xf);
+    if (norm_w) {
+      float g[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(norm_w) + c), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xf[e] = bf16_round(bf16_round(xf[e] * inv[m]) * g[e]);
+    }
+  }
+};
+
+// inv[m] = rsqrt(mean(x[m]^2) + eps) of the M rows, block-wide (every thread of the block calls it)
+template <int M>
+WGKV_DEV void block_rms_inv(const uint16_t* x, int64_t xs, int k, float eps, float* inv) {
+  __shared__ float red[kSgWarps][M];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < k / 8; c += kSgWarps * 32) {
+      float f[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+    if (lane == 0) red[warp][m] = ss;
+  }
+  __syncthreads();
+  if (threadIdx.x < M) {
+    float t = 0.f;
+    for (int w = 0; w < kSgWarps; ++w) t += red[w][threadIdx.x];
+    inv[threadIdx.x] = rsqrtf(t / float(k) + eps);
+  }
+  __syncthreads();
+}
+
+// acc[m] += sum over chunks [c, c1) of this lane (stride 32) of x[m] . w_row; wv holds the first pass
+template <int M>
+WGKV_DEV void dot_rows(const uint4* wr, int cfirst, int c1, const XRows<M>& X, uint4 (&wv)[kSgUnroll],
+                       bool preloaded, float (&acc)[M]) {
+  for (int cb = cfirst; cb < c1; cb += 32 * kSgUnroll) {
+    if (!preloaded || cb != cfirst) {
+#pragma unroll
+      for (int u = 0; u < kSgUnroll; ++u)
+        wv[u] = cb + 32 * u < c1 ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);  // streamed once
+    }
+#pragma unroll
+    for (int u = 0; u < kSgUnroll; ++u) {
+      const int c = cb + 32 * u;
+      if (c >= c1) break;
+      float wf[8];
+      unpack8(wv[u], wf);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float xf[8];
+        X.load(m, c, xf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], wf[e], acc[m]);
+      }
+    }
+  }
+}
+
 template <int M>
 __global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16_t* __restrict__ x, int64_t xs,
                                                                     const uint16_t* __restrict__ w, int n, int k,
                                                                     int rpb, void* y, int64_t ys, int out_f32,
-                                                                    const uint16_t* res, int64_t rs) {
+                                                                    const uint16_t* res, int64_t rs,
+                                                                    const uint16_t* norm_w, float eps) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = kSgWarps / rpb;          // warps per row
   const int row_in = warp % rpb, slice = warp / rpb;
@@ -113,6 +187,7 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16
   const int kc = k / 8;                   // 16-byte chunks per row
   const int per = (kc + ks - 1) / ks;     // chunks per slice
   const int c0 = slice * per, c1 = min(kc, c0 + per);
+  __shared__ float inv[M];
   float acc[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) acc[m] = 0.f;
@@ -126,29 +201,9 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16
     wv[u] = row < n && c < c1 ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
   }
   griddep_wait();
-  if (row < n) {
-    for (int cb = c0 + lane; cb < c1; cb += 32 * kSgUnroll) {
-      if (cb != c0 + lane) {
-#pragma unroll
-        for (int u = 0; u < kSgUnroll; ++u)
-          wv[u] = cb + 32 * u < c1 ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);  // streamed once
-      }
-#pragma unroll
-      for (int u = 0; u < kSgUnroll; ++u) {
-        const int c = cb + 32 * u;
-        if (c >= c1) break;
-        float wf[8];
-        unpack8(wv[u], wf);
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float xf[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), xf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], wf[e], acc[m]);
-        }
-      }
-    }
-  }
+  if (norm_w) block_rms_inv<M>(x, xs, k, eps, inv);
+  const XRows<M> X{x, xs, norm_w, inv};
+  if (row < n) dot_rows<M>(wr, c0 + lane, c1, X, wv, true, acc);
 #pragma unroll
   for (int m = 0; m < M; ++m)
     for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffff, acc[m], o);
@@ -173,58 +228,59 @@ __global__ void __launch_bounds__(kSgWarps * 32) skinny_gemm_kernel(const uint16
   }
 }
 
-// Many rows (n >= 8 * 4 * SMs): persistent warps, one row at a time, grid-stride over rows; no
-// block barrier.
+// Many rows (n >= 8 * 4 * SMs, or paired): persistent warps, one output row at a time, grid-stride;
+// no block barrier after the optional RMS prologue.  paired: w holds [gate (n/2 rows) | up (n/2
+// rows)] and output j = bf16(bf16(silu(bf16(g_j))) * bf16(u_j)) -- the MLP activation of
+// silu_mul_kernel fused into its projection.
 template <int M>
 __global__ void __launch_bounds__(kSgWarps * 32) skinny_rows_kernel(const uint16_t* __restrict__ x, int64_t xs,
                                                                     const uint16_t* __restrict__ w, int n, int k,
                                                                     void* y, int64_t ys, int out_f32,
-                                                                    const uint16_t* res, int64_t rs) {
+                                                                    const uint16_t* res, int64_t rs,
+                                                                    const uint16_t* norm_w, float eps, int paired) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kSgWarps + (threadIdx.x >> 5), nw = gridDim.x * kSgWarps;
   const int kc = k / 8;
+  const int n_out = paired ? n / 2 : n;
+  __shared__ float inv[M];
   griddep_launch();
   uint4 wv[kSgUnroll];
   {  // the first row's first pass of weight loads goes out before waiting for the previous kernel
-    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(min(gw, n - 1)) * k);
+    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(min(gw, n_out - 1)) * k);
 #pragma unroll
     for (int u = 0; u < kSgUnroll; ++u) {
       const int c = lane + 32 * u;
-      wv[u] = gw < n && c < kc ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
+      wv[u] = gw < n_out && c < kc ? __ldcs(wr + c) : make_uint4(0, 0, 0, 0);
     }
   }
   griddep_wait();
-  for (int row = gw; row < n; row += nw) {
-    const uint4* wr = reinterpret_cast<const uint4*>(w + int64_t(row) * k);
+  if (norm_w) block_rms_inv<M>(x, xs, k, eps, inv);
+  const XRows<M> X{x, xs, norm_w, inv};
+  for (int row = gw; row < n_out; row += nw) {
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0.f;
-    for (int cb = lane; cb < kc; cb += 32 * kSgUnroll) {
-      if (row != gw || cb != lane) {
+    dot_rows<M>(reinterpret_cast<const uint4*>(w + int64_t(row) * k), lane, kc, X, wv, row == gw, acc);
 #pragma unroll
-        for (int u = 0; u < kSgUnroll; ++u)
-          wv[u] = cb + 32 * u < kc ? __ldcs(wr + cb + 32 * u) : make_uint4(0, 0, 0, 0);
-      }
+    for (int m = 0; m < M; ++m)
+      for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffff, acc[m], o);
+    if (paired) {
+      float up[M];
 #pragma unroll
-      for (int u = 0; u < kSgUnroll; ++u) {
-        const int c = cb + 32 * u;
-        if (c >= kc) break;
-        float wf[8];
-        unpack8(wv[u], wf);
+      for (int m = 0; m < M; ++m) up[m] = 0.f;
+      dot_rows<M>(reinterpret_cast<const uint4*>(w + int64_t(row + n_out) * k), lane, kc, X, wv, false, up);
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float xf[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(x + m * xs) + c), xf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], wf[e], acc[m]);
-        }
+      for (int m = 0; m < M; ++m) {
+        float u = up[m];
+        for (int o = 16; o; o >>= 1) u += __shfl_xor_sync(0xffffffff, u, o);
+        const float g = bf16_round(acc[m]);
+        acc[m] = bf16_round(g / (1.f + expf(-g))) * bf16_round(u);
       }
     }
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      float v = acc[m];
-      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
       if (lane == m) {
+        float v = acc[m];
         if (res) v += bf2f(res[m * rs + row]);
         if (out_f32) reinterpret_cast<float*>(y)[m * ys + row] = v;
         else reinterpret_cast<uint16_t*>(y)[m * ys + row] = f2bf(v);
@@ -316,24 +372,25 @@ extern "C" int wgkv_silu_mul(const uint16_t* gate_up, int64_t gu_stride, int row
 
 extern "C" int wgkv_skinny_gemm(const uint16_t* x, int64_t x_stride, int m, const uint16_t* w, int n, int k, void* y,
                                 int64_t y_stride, int out_f32, const uint16_t* residual, int64_t r_stride,
-                                void* stream) {
+                                const uint16_t* rms_weight, float rms_eps, int paired, void* stream) {
   if (!x || !w || !y || m <= 0 || m > 8 || n <= 0 || k <= 0 || k % 8 || x_stride % 8 || !aligned16(x) ||
-      !aligned16(w) || (residual && out_f32))
+      !aligned16(w) || (residual && out_f32) || (rms_weight && !aligned16(rms_weight)))
     return WGKV_EINVAL;
+  if (paired && (n % 2 || out_f32 || residual)) return WGKV_EINVAL;
   const int sms = device_sms();
   if (sms <= 0) return WGKV_ECUDA;
   // rows per block: as many as keep >= 4 blocks per SM; the block's other warps split K
   int rpb = 1;
   while (rpb < kSgWarps && int64_t(n) / (rpb * 2) >= 4 * sms) rpb *= 2;
-  const bool rows = rpb == kSgWarps && int64_t(n) >= int64_t(kSgWarps) * 8 * sms;
+  const bool rows = paired || (rpb == kSgWarps && int64_t(n) >= int64_t(kSgWarps) * 8 * sms);
   const int blocks = rows ? 8 * sms : (n + rpb - 1) / rpb;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
 #define WGKV_SG(MM)                                                                                            \
   e = rows ? launch_pdl(skinny_rows_kernel<MM>, dim3(blocks), dim3(kSgWarps * 32), 0, s, x, x_stride, w, n, k, y,  \
-                        y_stride, out_f32, residual, r_stride)                                                 \
+                        y_stride, out_f32, residual, r_stride, rms_weight, rms_eps, paired)                     \
            : launch_pdl(skinny_gemm_kernel<MM>, dim3(blocks), dim3(kSgWarps * 32), 0, s, x, x_stride, w, n, k,     \
-                        rpb, y, y_stride, out_f32, residual, r_stride)
+                        rpb, y, y_stride, out_f32, residual, r_stride, rms_weight, rms_eps)
   switch (m) {
     case 1: WGKV_SG(1); break;
     case 2: WGKV_SG(2); break;

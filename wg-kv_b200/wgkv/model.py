@@ -79,9 +79,11 @@ def silu_mul(gu):
     return out
 
 
-def skinny_linear(x, w, residual=None, out_f32=False):
+def skinny_linear(x, w, residual=None, out_f32=False, rms_weight=None, rms_eps=1e-6, paired=False):
     """``wgkv_skinny_gemm``: x (m <= 8, k) bf16 @ w (n, k)^T, fp32 accumulate; ``residual`` (m, n)
-    bf16 is added and receives the result in place; ``out_f32`` returns fp32 (no residual)."""
+    bf16 is added and receives the result in place; ``out_f32`` returns fp32 (no residual);
+    ``rms_weight`` RMS-normalises x first (as :func:`rms_norm`); ``paired`` treats w as
+    [gate | up] and returns silu(x gate^T) * (x up^T) (as :func:`silu_mul` on the projection)."""
     m, k = x.shape
     n = w.shape[0]
     assert x.stride(1) == 1 and w.is_contiguous() and m <= 8
@@ -89,11 +91,12 @@ def skinny_linear(x, w, residual=None, out_f32=False):
         y = residual
         assert y.stride(1) == 1 and y.shape == (m, n)
     else:
-        y = torch.empty(m, n, dtype=torch.float32 if out_f32 else x.dtype, device=x.device)
+        y = torch.empty(m, n // 2 if paired else n, dtype=torch.float32 if out_f32 else x.dtype, device=x.device)
     check(lib.wgkv_skinny_gemm(x.data_ptr(), x.stride(0), m, w.data_ptr(), n, k, y.data_ptr(), y.stride(0),
                                int(out_f32), residual.data_ptr() if residual is not None else None,
-                               residual.stride(0) if residual is not None else 0, stream_ptr(x.device)),
-          "wgkv_skinny_gemm")
+                               residual.stride(0) if residual is not None else 0,
+                               rms_weight.data_ptr() if rms_weight is not None else None, float(rms_eps), int(paired),
+                               stream_ptr(x.device)), "wgkv_skinny_gemm")
     return y
 
 
@@ -235,10 +238,10 @@ class WgkvDecoder:
         return self.fused and rows <= 8
 
     def _qkv_rows(self, L, x_in):
-        x = self._norm(x_in, L.in_norm)
-        if self._skinny(x.numel() // x.shape[-1]):
-            return skinny_linear(x.reshape(-1, x.shape[-1]), L.qkv).view(*x.shape[:-1], -1)
-        return x @ L.qkv.t()
+        if self._skinny(x_in.numel() // x_in.shape[-1]):  # the input norm runs inside the projection
+            return skinny_linear(x_in.reshape(-1, x_in.shape[-1]), L.qkv, rms_weight=L.in_norm,
+                                 rms_eps=self.s.rms_eps).view(*x_in.shape[:-1], -1)
+        return self._norm(x_in, L.in_norm) @ L.qkv.t()
 
     def _qkv(self, L, x_in):
         s = self.s
@@ -274,8 +277,9 @@ class WgkvDecoder:
         if self._skinny(h2.shape[0]):
             skinny_linear(a2, L.o, residual=h2)
             t = self._time("mlp")
-            x = rms_norm(h2, L.post_norm, self.s.rms_eps)
-            skinny_linear(silu_mul(skinny_linear(x, L.gate_up)), L.down, residual=h2)
+            # post-attention norm and SiLU(gate) * up inside the gate_up projection
+            act = skinny_linear(h2, L.gate_up, rms_weight=L.post_norm, rms_eps=self.s.rms_eps, paired=True)
+            skinny_linear(act, L.down, residual=h2)
         else:
             h2.addmm_(a2, L.o.t())
             t = self._time("mlp")
@@ -309,10 +313,11 @@ class WgkvDecoder:
             self._stop(t)
             h = self._after_attn(L, h, o.reshape(B, T, -1))
         t = self._time("lm_head")
-        x = self._norm(h[:, -1:].contiguous(), self.final_norm)
         if self._skinny(B):
-            logits = skinny_linear(x.view(B, -1), self.lm_head, out_f32=True)
+            logits = skinny_linear(h[:, -1].contiguous(), self.lm_head, out_f32=True, rms_weight=self.final_norm,
+                                   rms_eps=self.s.rms_eps)
         else:
+            x = self._norm(h[:, -1:].contiguous(), self.final_norm)
             logits = (x @ self.lm_head.t()).float()[:, 0]
         self._stop(t)
         return logits
