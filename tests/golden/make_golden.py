@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container where the reference checkout is available (default
-``/root/reference``; override with ``WGKV_REFERENCE``).  The reference's
+Run where a checkout of the reference is available (its location in the
+``WGKV_REFERENCE`` environment variable, or the default below).  The reference's
 ``src/modeling_layers.py`` is imported unmodified and driven on CPU:
 
 * ``GatingPredictor`` fast path (``:170-196``) -> admission scores / mask
