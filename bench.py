@@ -710,6 +710,114 @@ def c5_arm(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def quest_arm(args, rank, world, local_rank):
+    """C2 decode with QUEST page selection (use_quest, modeling_layers.py:452-576) under a token budget,
+    and one SnapKV eviction (snapkv_evict, :595-671) timed over the same pool."""
+    import torch
+    import wgkv
+    from wgkv.dist import max_over_ranks
+    from wgkv.pool import pool_ref
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    Ly, B, Hk, Hq, D = CFG["layers"], CFG["batch"], CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"]
+    W, T = CFG["window"], CFG["page"]
+    budget = args.quest_budget
+    cache, rate, glen0 = build_state(dev, args.warmup + args.steps + 8, seed=2 + 1000 * rank)
+    NB = cache.total_blocks
+    kp = cache.block_pool_k.view(NB, T, D)
+    cache.quest_block_key_min = torch.empty(NB, D, dtype=torch.bfloat16, device=dev)
+    cache.quest_block_key_max = torch.empty(NB, D, dtype=torch.bfloat16, device=dev)
+    for p0 in range(0, NB, 1 << 20):  # page key bounds of the synthetic pool (all 16 rows of each page)
+        p1 = min(NB, p0 + (1 << 20))
+        torch.amin(kp[p0:p1], dim=1, out=cache.quest_block_key_min[p0:p1])
+        torch.amax(kp[p0:p1], dim=1, out=cache.quest_block_key_max[p0:p1])
+    cache.wgkv_pool.quest_min = cache.quest_block_key_min.data_ptr()
+    cache.wgkv_pool.quest_max = cache.quest_block_key_max.data_ptr()
+    layers = build_layers(dev, rate, seed=3 + 1000 * rank)
+    for a in layers:
+        a.config.use_quest, a.config.quest_token_budget = True, budget
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    NI = 4
+    inputs = torch.randn(NI, Ly, B, 1, Hq + 3 * Hk, D, generator=g, device=dev).to(torch.bfloat16)
+
+    def step(s):
+        for l in range(Ly):
+            x = inputs[s % NI, l]
+            q = x[:, :, :Hq].transpose(1, 2)
+            k, v, pk = (x[:, :, Hq + i * Hk:Hq + (i + 1) * Hk].transpose(1, 2) for i in range(3))
+            layers[l].self_attn_forward_patch(layers[l], 3, None, cache, (B, 1), q, pk, k, v)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    wgkv.check_errors()
+    clk = ClockSampler(local_rank) if rank == 0 else None
+    l0 = wgkv.lib.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(args.steps):
+        step(s)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = wgkv.lib.launches - l0
+    clocks = clk.stop() if clk else None
+    wgkv.check_errors()
+    ms = max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
+    glen = cache.global_lengths.cpu().numpy().astype(np.int64)
+    full = W + glen
+    kept = np.minimum(full, W + ((budget - W + T - 1) // T) * T)  # tokens attended per head (upper bound)
+    attn_bytes = float(kept.sum()) * D * 2 * 2 + float((glen // T).sum()) * 2 * D * 2  # K/V read + page bounds
+    # ---- one SnapKV eviction over the whole pool ----
+    snap = None
+    if world == 1:
+        win, ratio, ks = 256, 0.3, 5
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(9)
+        qbuf = torch.randn(Ly, B, win, Hq, D, generator=gq, device=dev).to(torch.bfloat16)
+        free_ids = torch.zeros(NB, dtype=torch.int32, device=dev)
+        free_n = torch.zeros(1, dtype=torch.int32, device=dev)
+        cache.wgkv_pool.free_ids, cache.wgkv_pool.free_count = free_ids.data_ptr(), free_n.data_ptr()
+        nbytes = int(wgkv.lib.wgkv_snapkv_workspace_size(pool_ref(cache), win, Hq))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        before = int(cache.global_lengths.sum().item())
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record()
+        st = wgkv.lib.wgkv_snapkv_evict(pool_ref(cache), qbuf.data_ptr(), win, Hq, D ** -0.5, ratio, ks,
+                                        ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+        e3.record()
+        torch.cuda.synchronize()
+        assert st == 0
+        wgkv.check_errors()
+        after = int(cache.global_lengths.sum().item())
+        evict_ms = e2.elapsed_time(e3)
+        flops = 2.0 * 2 * win * (Hq // Hk) * D * before * 2  # two passes of window-queries x keys
+        snap = {"metric": "SnapKV eviction ms (all layers, whole pool)", "value": evict_ms, "unit": "ms",
+                "window": win, "evict_ratio": ratio, "kernel_size": ks, "tokens_before": before,
+                "tokens_after": after, "pages_freed": int(free_n.item()),
+                "score_tflops": flops / (evict_ms / 1e3) / 1e12,
+                "kernels": "snap_rowstats / snap_scores (mma.sync) + snap_select_compact + snap_free"}
+    peak, kind = peaks()
+    if rank == 0:
+        line = {
+            "metric": f"decode tok/s @128K ragged cache with QUEST (budget {budget} tokens / head)",
+            "value": world * B / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (page bounds over all rows of each page)",
+            "config": {"workload": "C2 decode + QUEST selection (use_quest)", "quest_token_budget": budget,
+                       "l2": "inputs larger than L2, no flush", **CFG},
+            "attended_tokens_per_head": float(kept.mean()), "cached_tokens_per_head": float(full.mean()),
+            "roofline": {"bound": "hbm", "kernel": "quest_select + paged_decode (whole step)",
+                         "achieved": attn_bytes / (ms / 1e3) / 1e9, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                         "frac": attn_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None},
+            "gpu_launches": launches, "clocks": clocks,
+        }
+        if snap is not None:
+            line["snapkv_evict"] = snap
+        print(json.dumps(line), flush=True)
+
+
 def model_arm(args, rank, world, local_rank):
     """TTFT / TPOT of a whole random-init decoder on the WG-KV path (scripts/profiling.py:346-418)."""
     import torch
@@ -828,7 +936,8 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wgkv", choices=["wgkv", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode", "c5_decode", "model"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "qwen3_decode", "c5_decode", "model", "quest_decode"])
+    ap.add_argument("--quest-budget", type=int, default=8192, help="quest_decode workload: tokens kept per head")
     ap.add_argument("--model", default="llama-3.2-1b", help="model workload: llama-3.2-1b | llama-3.1-8b | qwen3-4b")
     ap.add_argument("--prompt", type=int, default=32000, help="model workload: prompt length")
     ap.add_argument("--batch", type=int, default=1, help="model workload: sequences")
@@ -864,6 +973,8 @@ def main():
             c5_arm(args, rank, world, local_rank)
         elif args.workload == "model":
             model_arm(args, rank, world, local_rank)
+        elif args.workload == "quest_decode":
+            quest_arm(args, rank, world, local_rank)
         else:
             gpu_arm(args, rank, world, local_rank)
     finally:

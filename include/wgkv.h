@@ -233,12 +233,14 @@ WGKV_API int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_p
  * out_table (B, Hk, out_stride) = their page ids, ring pages first, then the global pages in
  * position order -- inputs for wgkv_paged_decode.  q (B, q_heads, D) bf16, rows q_sb elements apart.
  * cur_local_len = WGKV_RING_ON_DEVICE takes the ring length from pool->ring_state.  out_stride must
- * be at least wgkv_quest_table_stride(window, page, token_budget, max_blocks_per_head).
+ * be at least wgkv_quest_table_stride(window, page, token_budget, max_blocks_per_head); workspace of
+ * wgkv_quest_workspace_size(pool) bytes (page score keys).
  */
 WGKV_API size_t wgkv_quest_table_stride(int window, int page, int token_budget, int max_blocks_per_head);
+WGKV_API size_t wgkv_quest_workspace_size(const wgkv_pool* pool);
 WGKV_API int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local_len, const uint16_t* q, int64_t q_sb,
                                int q_heads, int token_budget, int32_t* out_seqlens, int32_t* out_table,
-                               int64_t out_stride, void* stream);
+                               int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- SnapKV eviction (snapkv_enabled) ------------------------------------- */
 /*

@@ -8,8 +8,9 @@
 // head keeps its ring pages, the `capacity - 1` best full global pages (all of them if they fit)
 // and its trailing partial page, within a token budget.
 //
-// Selection: scores become order-preserving 16-bit keys in shared memory; a two-pass 8-bit radix
-// histogram finds the k-th largest key; pages above it are taken, and among pages equal to it the
+// Two kernels: the page scores (one CTA per 64 pages of a head, four pages' bounds in flight per
+// warp) become order-preserving 16-bit keys in a workspace; per head, a two-pass 8-bit radix
+// histogram over them finds the k-th largest key; pages above it are taken, and among pages equal to it the
 // lowest positions (torch.topk leaves the order of ties unspecified).  The chosen pages are written
 // in ascending position order after the ring pages (attention does not depend on the order).
 #include "common.cuh"
@@ -47,29 +48,102 @@ struct QuestArgs {
   wgkv_pool P;
 };
 
-__global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, int layer, int cur, const uint16_t* q,
-                                                                  int64_t q_sb, int Hq, int budget, int32_t* out_sl,
-                                                                  int32_t* out_tab, int64_t out_stride) {
+// the per-head selection sizes of quest_select_blocks (:478-512)
+struct QuestHead {
+  int local_blocks, full, rem, cap, full_cap;
+  WGKV_DEV QuestHead(const wgkv_pool& P, int layer, int bh, int cur, int budget) {
+    const int T = P.page;
+    local_blocks = (cur + T - 1) / T;
+    const int rest = budget - cur;
+    const int budget_blocks = ((rest > 0 ? rest : 0) + T - 1) / T;
+    const int glen = P.global_lengths[int64_t(layer) * P.batch * P.kv_heads + bh];
+    full = glen / T;
+    rem = glen - full * T;
+    cap = min(budget_blocks, full + (rem > 0));
+    full_cap = cap > 0 ? cap - (rem > 0) : 0;
+  }
+  WGKV_DEV bool ranks() const { return full_cap > 0 && full > 0 && full_cap < full; }
+};
+
+WGKV_DEV int resolve_cur(const wgkv_pool& P, int cur) {
+  if (cur >= 0) return cur;
+  const int len = P.ring_state[0];  // device ring: the length after this step's append (:1390-1396)
+  return len < P.window ? len + 1 : P.window;
+}
+
+constexpr int kQsPagesPerCta = 64;
+constexpr int kQsBatch = 4;  // pages whose bound loads a warp keeps in flight
+
+// Page scores of every head that has to rank its pages: one warp per page, four pages per pass,
+// D / 32 dimensions per lane; writes order-preserving 16-bit keys to keys[bh][position].
+template <int D>
+__global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, int layer, int cur, const uint16_t* q,
+                                                                 int64_t q_sb, int Hq, int budget, uint16_t* keys,
+                                                                 int key_stride) {
+  const wgkv_pool& P = qa.P;
+  const int Hk = P.kv_heads, BH = P.batch * Hk;
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk, G = Hq / Hk;
+  cur = resolve_cur(P, cur);
+  const QuestHead H(P, layer, bh, cur, budget);
+  const int p0 = blockIdx.x * kQsPagesPerCta;
+  if (!H.ranks() || p0 >= H.full) return;
+  constexpr int E = D / 32;  // dimensions per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float qv[16][E];
+  const uint16_t* qh = q + int64_t(b) * q_sb + int64_t(h) * G * D + lane * E;
+#pragma unroll
+  for (int g = 0; g < 16; ++g)
+#pragma unroll
+    for (int e = 0; e < E; ++e) qv[g][e] = g < G ? bf2f(qh[g * D + e]) : 0.f;
+  const int32_t* grow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page;
+  const int p1 = min(H.full, p0 + kQsPagesPerCta);
+  for (int pb = p0 + warp * kQsBatch; pb < p1; pb += kQsWarps * kQsBatch) {
+    uint16_t mn[kQsBatch][E], mx[kQsBatch][E];
+#pragma unroll
+    for (int j = 0; j < kQsBatch; ++j) {
+      const int pos = pb + j < p1 ? pb + j : p1 - 1;
+      const int64_t pid = grow[pos];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        mn[j][e] = P.quest_min[pid * D + lane * E + e];
+        mx[j][e] = P.quest_max[pid * D + lane * E + e];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kQsBatch; ++j) {
+      float best = -INFINITY;
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {
+        if (g >= G) break;
+        float sum = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float x = qv[g][e];
+          sum += bf16_round(x * bf2f(x >= 0.f ? mx[j][e] : mn[j][e]));
+        }
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+        best = fmaxf(best, bf16_round(sum));
+      }
+      if (lane == 0 && pb + j < p1) keys[int64_t(bh) * key_stride + pb + j] = uint16_t(score_key(f2bf(best)));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, int layer, int cur, int budget,
+                                                                  const uint16_t* gkeys, int key_stride,
+                                                                  int32_t* out_sl, int32_t* out_tab,
+                                                                  int64_t out_stride) {
   const wgkv_pool& P = qa.P;
   extern __shared__ __align__(16) uint8_t qs_smem[];
-  const int Hk = P.kv_heads, BH = P.batch * Hk, D = P.head_dim, T = P.page, W = P.window;
-  const int bh = blockIdx.x, b = bh / Hk, h = bh - b * Hk, G = Hq / Hk;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hk = P.kv_heads, BH = P.batch * Hk, T = P.page, W = P.window;
+  const int bh = blockIdx.x;
+  const int tid = threadIdx.x;
   __shared__ int hist[256];
   __shared__ int wsum[kQsWarps];
   __shared__ int s_bin, s_take;
-  if (cur < 0) {  // device ring position: the length after this step's append (decode_wrapper :1390-1396)
-    const int len = P.ring_state[0];
-    cur = len < W ? len + 1 : W;
-  }
-  const int local_blocks = (cur + T - 1) / T;
-  const int rest = budget - cur;
-  const int budget_blocks = ((rest > 0 ? rest : 0) + T - 1) / T;
-  const int glen = P.global_lengths[int64_t(layer) * BH + bh];
-  const int full = glen / T, rem = glen - full * T;
-  const int nb = full + (rem > 0);
-  const int cap = min(budget_blocks, nb);
-  const int full_cap = cap > 0 ? cap - (rem > 0) : 0;
+  cur = resolve_cur(P, cur);
+  const QuestHead H(P, layer, bh, cur, budget);
+  const int local_blocks = H.local_blocks, full = H.full, full_cap = H.full_cap;
   const int32_t* trow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head;
   const int32_t* grow = trow + W / T;
   int32_t* orow = out_tab + int64_t(bh) * out_stride;
@@ -80,28 +154,9 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
       for (int i = tid; i < full; i += kQsThreads) orow[local_blocks + i] = grow[i];
       nsel = full;
     } else {
-      float* qv = reinterpret_cast<float*>(qs_smem);             // [G][D]
-      uint16_t* keys = reinterpret_cast<uint16_t*>(qv + G * D);  // [full]
-      const uint16_t* qh = q + int64_t(b) * q_sb + int64_t(h) * G * D;
-      for (int i = tid; i < G * D; i += kQsThreads) qv[i] = bf2f(qh[i]);
+      uint16_t* keys = reinterpret_cast<uint16_t*>(qs_smem);  // [full]
+      for (int i = tid; i < full; i += kQsThreads) keys[i] = gkeys[int64_t(bh) * key_stride + i];
       __syncthreads();
-      // ---- page scores: one warp per page ----
-      for (int pos = warp; pos < full; pos += kQsWarps) {
-        const int64_t pid = grow[pos];
-        const uint16_t* mn = P.quest_min + pid * D;
-        const uint16_t* mx = P.quest_max + pid * D;
-        float best = -INFINITY;
-        for (int g = 0; g < G; ++g) {
-          float s = 0.f;
-          for (int c = lane; c < D; c += 32) {
-            const float x = qv[g * D + c];
-            s += bf16_round(x * bf2f(x >= 0.f ? mx[c] : mn[c]));
-          }
-          for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
-          best = fmaxf(best, bf16_round(s));
-        }
-        if (lane == 0) keys[pos] = uint16_t(score_key(f2bf(best)));
-      }
       // ---- k-th largest key: two 8-bit radix passes ----
       int need = full_cap;  // keys still to take at or below the current prefix
       uint32_t prefix = 0;
@@ -153,9 +208,9 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
   }
   if (tid == 0) {
     int tokens = cur + nsel * T;
-    if (cap > 0 && rem > 0) {  // the trailing partial page is always kept when there is room
+    if (H.cap > 0 && H.rem > 0) {  // the trailing partial page is always kept when there is room
       orow[local_blocks + nsel] = grow[full];
-      tokens += rem;
+      tokens += H.rem;
     }
     out_sl[bh] = tokens;
   }
@@ -174,18 +229,24 @@ extern "C" size_t wgkv_quest_table_stride(int window, int page, int token_budget
   return size_t(lb + (bb < g ? bb : g > 0 ? g : 0));
 }
 
+extern "C" size_t wgkv_quest_workspace_size(const wgkv_pool* pool) {
+  if (!pool) return 0;
+  return size_t(pool->batch) * pool->kv_heads * size_t(pool->max_blocks_per_head) * 2 + 256;
+}
+
 extern "C" int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local_len, const uint16_t* q, int64_t q_sb,
                                  int q_heads, int token_budget, int32_t* out_seqlens, int32_t* out_table,
-                                 int64_t out_stride, void* stream) {
-  if (!pool || !pool->quest_min || !pool->quest_max || !q || !out_seqlens || !out_table || layer < 0 ||
-      layer >= pool->layers || q_heads <= 0 || q_heads % pool->kv_heads || q_heads / pool->kv_heads > 16)
+                                 int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!pool || !pool->quest_min || !pool->quest_max || !q || !out_seqlens || !out_table || !workspace ||
+      layer < 0 || layer >= pool->layers || q_heads <= 0 || q_heads % pool->kv_heads ||
+      q_heads / pool->kv_heads > 16)
     return WGKV_EINVAL;
   if (cur_local_len == WGKV_RING_ON_DEVICE ? !pool->ring_state : (cur_local_len <= 0 || cur_local_len > pool->window))
     return WGKV_EINVAL;
   if (out_stride < int64_t(wgkv_quest_table_stride(pool->window, pool->page, token_budget, pool->max_blocks_per_head)))
     return WGKV_EINVAL;
-  const int G = q_heads / pool->kv_heads;
-  const size_t smem = size_t(G) * pool->head_dim * 4 + size_t(pool->max_blocks_per_head) * 2 + 16;
+  if (workspace_bytes < wgkv_quest_workspace_size(pool)) return WGKV_ENOSPC;
+  const size_t smem = size_t(pool->max_blocks_per_head) * 2 + 16;
   constexpr size_t kMaxDyn = 200 * 1024;  // plus ~1 KB of static shared memory
   if (smem > kMaxDyn) return WGKV_EINVAL;
   static bool attr[64] = {false};
@@ -198,7 +259,16 @@ extern "C" int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local
     attr[dev] = true;
   }
   QuestArgs qa{*pool};
-  quest_select_kernel<<<pool->batch * pool->kv_heads, kQsThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      qa, layer, cur_local_len, q, q_sb, q_heads, token_budget, out_seqlens, out_table, out_stride);
+  const int BH = pool->batch * pool->kv_heads;
+  uint16_t* keys = static_cast<uint16_t*>(workspace);
+  const int ks = pool->max_blocks_per_head;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 g1((pool->max_blocks_per_head + kQsPagesPerCta - 1) / kQsPagesPerCta, BH);
+  if (pool->head_dim == 128)
+    quest_score_kernel<128><<<g1, kQsThreads, 0, s>>>(qa, layer, cur_local_len, q, q_sb, q_heads, token_budget, keys, ks);
+  else
+    quest_score_kernel<64><<<g1, kQsThreads, 0, s>>>(qa, layer, cur_local_len, q, q_sb, q_heads, token_budget, keys, ks);
+  quest_select_kernel<<<BH, kQsThreads, smem, s>>>(qa, layer, cur_local_len, token_budget, keys, ks, out_seqlens,
+                                                   out_table, out_stride);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

@@ -179,9 +179,10 @@ def quest_select_blocks(self, query_states, past_key_value, local_blocks_per_hea
     stride = int(lib.wgkv_quest_table_stride(s.window, s.page, int(c.quest_token_budget), s.max_blocks_per_head))
     seqlens = torch.empty(B, s.kv_heads, dtype=torch.int32, device=device)
     table = torch.empty(B, s.kv_heads, stride, dtype=torch.int32, device=device)
+    ws = workspace(device, "quest", int(lib.wgkv_quest_workspace_size(pool_ref(past_key_value))))
     st = lib.wgkv_quest_select(pool_ref(past_key_value), self.layer_idx, int(local_tokens_total), q.data_ptr(),
                                q.stride(0), Hq, int(c.quest_token_budget), seqlens.data_ptr(), table.data_ptr(),
-                               stride, stream_ptr(device))
+                               stride, ws.data_ptr(), ws.numel(), stream_ptr(device))
     check(st, "wgkv_quest_select")
     return seqlens, table
 
