@@ -463,18 +463,34 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
       vd[c] = vs[c];
     }
     if (P.quest_min) {  // page key bounds (:744-761): a new page starts at the key
-      uint16_t* mn = P.quest_min + int64_t(pid) * D;
-      uint16_t* mx = P.quest_max + int64_t(pid) * D;
-      const uint16_t* kk = P.k + src * D;
-      for (int c = 0; c < D; ++c) {
-        const uint16_t kb = kk[c];
-        if (gl % T == 0) {
-          mn[c] = kb;
-          mx[c] = kb;
+      uint4* mn = reinterpret_cast<uint4*>(P.quest_min + int64_t(pid) * D);
+      uint4* mx = reinterpret_cast<uint4*>(P.quest_max + int64_t(pid) * D);
+      const bool fresh = gl % T == 0;
+#pragma unroll 4
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 kv = ks[c];
+        if (fresh) {
+          mn[c] = kv;
+          mx[c] = kv;
         } else {
-          const float x = bf2f(kb);
-          if (x < bf2f(mn[c])) mn[c] = kb;
-          if (x > bf2f(mx[c])) mx[c] = kb;
+          const uint4 a = mn[c], z = mx[c];
+          const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, aw[4] = {a.x, a.y, a.z, a.w}, zw[4] = {z.x, z.y, z.z, z.w};
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {  // two bf16 per word: keep each half's min / max bits
+            uint32_t l = 0, u = 0;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const uint32_t sh = 16 * half;
+              const uint16_t kb = uint16_t(kw[e] >> sh), ab = uint16_t(aw[e] >> sh), zb = uint16_t(zw[e] >> sh);
+              l |= uint32_t(bf2f(kb) < bf2f(ab) ? kb : ab) << sh;
+              u |= uint32_t(bf2f(kb) > bf2f(zb) ? kb : zb) << sh;
+            }
+            lo[e] = l;
+            hi[e] = u;
+          }
+          mn[c] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          mx[c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
       }
     }

@@ -121,6 +121,16 @@ WGKV_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn
 
 WGKV_DEV float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
 
+// the 8 bf16 values of a 16-byte vector as floats
+WGKV_DEV void unpack8(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    f[2 * e] = __uint_as_float(w[e] << 16);
+    f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+  }
+}
+
 // bf16 bit pattern of x (round to nearest even)
 WGKV_DEV uint16_t f2bf(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
 

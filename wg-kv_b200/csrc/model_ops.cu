@@ -14,15 +14,6 @@ namespace {
 
 constexpr int kRowThreads = 256;
 
-WGKV_DEV void unpack8(const uint4& u, float* f) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    f[2 * e] = __uint_as_float(w[e] << 16);
-    f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-  }
-}
-
 WGKV_DEV uint4 pack8(const float* f) {
   uint4 u;
   u.x = pack_bf16x2(f[0], f[1]);

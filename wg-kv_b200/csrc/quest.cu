@@ -71,11 +71,11 @@ WGKV_DEV int resolve_cur(const wgkv_pool& P, int cur) {
   return len < P.window ? len + 1 : P.window;
 }
 
-constexpr int kQsPagesPerCta = 64;
-constexpr int kQsBatch = 4;  // pages whose bound loads a warp keeps in flight
+constexpr int kQsPagesPerCta = kQsThreads;  // one page per thread
 
-// Page scores of every head that has to rank its pages: one warp per page, four pages per pass,
-// D / 32 dimensions per lane; writes order-preserving 16-bit keys to keys[bh][position].
+// Page scores of every head that has to rank its pages: one thread per page, streaming the page's
+// min / max rows with 16-byte loads against the group's queries in shared memory (broadcast reads);
+// writes order-preserving 16-bit keys to keys[bh][position].
 template <int D>
 __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, int layer, int cur, const uint16_t* q,
                                                                  int64_t q_sb, int Hq, int budget, uint16_t* keys,
@@ -87,46 +87,49 @@ __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, i
   const QuestHead H(P, layer, bh, cur, budget);
   const int p0 = blockIdx.x * kQsPagesPerCta;
   if (!H.ranks() || p0 >= H.full) return;
-  constexpr int E = D / 32;  // dimensions per lane
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float qv[16][E];
-  const uint16_t* qh = q + int64_t(b) * q_sb + int64_t(h) * G * D + lane * E;
+  __shared__ float qv[16 * D];  // [g][d]
+  const uint16_t* qh = q + int64_t(b) * q_sb + int64_t(h) * G * D;
+  for (int i = threadIdx.x; i < G * D; i += kQsThreads) qv[i] = bf2f(qh[i]);
+  __syncthreads();
+  const int pos = p0 + threadIdx.x;
+  if (pos >= H.full) return;
+  const int64_t pid = P.block_table[(int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page + pos];
+  const uint4* mn4 = reinterpret_cast<const uint4*>(P.quest_min + pid * D);
+  const uint4* mx4 = reinterpret_cast<const uint4*>(P.quest_max + pid * D);
+  float sum[16];
 #pragma unroll
-  for (int g = 0; g < 16; ++g)
+  for (int g = 0; g < 16; ++g) sum[g] = 0.f;
+  constexpr int kC = 4;  // 16-byte chunks of each bound row in flight per pass
+#pragma unroll 1
+  for (int c0 = 0; c0 < D / 8; c0 += kC) {
+    uint4 lo[kC], hi[kC];
 #pragma unroll
-    for (int e = 0; e < E; ++e) qv[g][e] = g < G ? bf2f(qh[g * D + e]) : 0.f;
-  const int32_t* grow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page;
-  const int p1 = min(H.full, p0 + kQsPagesPerCta);
-  for (int pb = p0 + warp * kQsBatch; pb < p1; pb += kQsWarps * kQsBatch) {
-    uint16_t mn[kQsBatch][E], mx[kQsBatch][E];
-#pragma unroll
-    for (int j = 0; j < kQsBatch; ++j) {
-      const int pos = pb + j < p1 ? pb + j : p1 - 1;
-      const int64_t pid = grow[pos];
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        mn[j][e] = P.quest_min[pid * D + lane * E + e];
-        mx[j][e] = P.quest_max[pid * D + lane * E + e];
-      }
+    for (int c = 0; c < kC; ++c) {
+      lo[c] = __ldg(mn4 + c0 + c);
+      hi[c] = __ldg(mx4 + c0 + c);
     }
 #pragma unroll
-    for (int j = 0; j < kQsBatch; ++j) {
-      float best = -INFINITY;
+    for (int c = 0; c < kC; ++c) {
+      float fl[8], fh[8];
+      unpack8(lo[c], fl);
+      unpack8(hi[c], fh);
 #pragma unroll
       for (int g = 0; g < 16; ++g) {
         if (g >= G) break;
-        float sum = 0.f;
+        const float* qg = qv + g * D + (c0 + c) * 8;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float x = qv[g][e];
-          sum += bf16_round(x * bf2f(x >= 0.f ? mx[j][e] : mn[j][e]));
+        for (int e = 0; e < 8; ++e) {
+          const float x = qg[e];
+          sum[g] += bf16_round(x * (x >= 0.f ? fh[e] : fl[e]));
         }
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
-        best = fmaxf(best, bf16_round(sum));
       }
-      if (lane == 0 && pb + j < p1) keys[int64_t(bh) * key_stride + pb + j] = uint16_t(score_key(f2bf(best)));
     }
   }
+  float best = -INFINITY;
+#pragma unroll
+  for (int g = 0; g < 16; ++g)
+    if (g < G) best = fmaxf(best, bf16_round(sum[g]));
+  keys[int64_t(bh) * key_stride + pos] = uint16_t(score_key(f2bf(best)));
 }
 
 __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, int layer, int cur, int budget,
