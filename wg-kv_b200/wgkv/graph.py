@@ -22,6 +22,13 @@ import torch
 from .pool import advance_host_ring, ring_to_device
 
 
+def graph_variant(local_length: int, local_ptr: int, window: int, defer: bool) -> str:
+    """Which captured step replays next: "refresh" when deferred gating rescores the whole ring on
+    this step (its insert position is window - 1, modeling_layers.py:1404-1405), else "plain"."""
+    ins = local_length if local_length < window else local_ptr
+    return "refresh" if defer and ins == window - 1 else "plain"
+
+
 class DecodeGraph:
     """Capture ``step_fn`` (one decode step of all layers over static input tensors) and replay it.
 
@@ -41,10 +48,6 @@ class DecodeGraph:
         self.graphs = {}
         self.out = {}
         self.pool = None
-
-    def _insert_pos(self):
-        c = self.cache
-        return c.local_length if c.local_length < self.W else c.local_ptr
 
     def capture(self, step_fn):
         c = self.cache
@@ -77,7 +80,7 @@ class DecodeGraph:
 
     def replay(self):
         """One decode step; returns what ``step_fn`` returned at capture (the graph's outputs)."""
-        name = "refresh" if self.defer and self._insert_pos() == self.W - 1 else "plain"
+        name = graph_variant(self.cache.local_length, self.cache.local_ptr, self.W, self.defer)
         self.graphs[name].replay()
         advance_host_ring(self.cache, self.W)
         return self.out[name]
