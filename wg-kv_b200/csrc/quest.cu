@@ -87,9 +87,17 @@ __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, i
   const QuestHead H(P, layer, bh, cur, budget);
   const int p0 = blockIdx.x * kQsPagesPerCta;
   if (!H.ranks() || p0 >= H.full) return;
-  __shared__ float qv[16 * D];  // [g][d]
-  const uint16_t* qh = q + int64_t(b) * q_sb + int64_t(h) * G * D;
-  for (int i = threadIdx.x; i < G * D; i += kQsThreads) qv[i] = bf2f(qh[i]);
+  // queries as bf16 pairs, and per pair a mask selecting min (q < 0) or max (q >= 0, -0 included)
+  __shared__ uint32_t q2[16 * D / 2];
+  __shared__ uint32_t neg[16 * D / 2];
+  const uint32_t* qh = reinterpret_cast<const uint32_t*>(q + int64_t(b) * q_sb + int64_t(h) * G * D);
+  for (int i = threadIdx.x; i < G * D / 2; i += kQsThreads) {
+    const uint32_t v = qh[i];
+    q2[i] = v;
+    const uint32_t lo_neg = (v & 0x8000u) && (v & 0x7FFFu) ? 0x0000FFFFu : 0u;
+    const uint32_t hi_neg = (v & 0x80000000u) && (v & 0x7FFF0000u) ? 0xFFFF0000u : 0u;
+    neg[i] = lo_neg | hi_neg;
+  }
   __syncthreads();
   const int pos = p0 + threadIdx.x;
   if (pos >= H.full) return;
@@ -110,17 +118,22 @@ __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, i
     }
 #pragma unroll
     for (int c = 0; c < kC; ++c) {
-      float fl[8], fh[8];
-      unpack8(lo[c], fl);
-      unpack8(hi[c], fh);
+      const uint32_t lw[4] = {lo[c].x, lo[c].y, lo[c].z, lo[c].w};
+      const uint32_t hw[4] = {hi[c].x, hi[c].y, hi[c].z, hi[c].w};
 #pragma unroll
       for (int g = 0; g < 16; ++g) {
         if (g >= G) break;
-        const float* qg = qv + g * D + (c0 + c) * 8;
+        const int base = g * (D / 2) + (c0 + c) * 4;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float x = qg[e];
-          sum[g] += bf16_round(x * (x >= 0.f ? fh[e] : fl[e]));
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t m = neg[base + e];
+          const uint32_t sel = (hw[e] & ~m) | (lw[e] & m);
+          // bf16(q * bound) for both halves: one round-to-nearest bf16x2 multiply
+          const __nv_bfloat162 pr = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&q2[base + e]),
+                                            *reinterpret_cast<const __nv_bfloat162*>(&sel));
+          const uint32_t pu = *reinterpret_cast<const uint32_t*>(&pr);
+          sum[g] += __uint_as_float(pu << 16);
+          sum[g] += __uint_as_float(pu & 0xffff0000u);
         }
       }
     }
