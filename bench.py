@@ -378,21 +378,49 @@ def gpu_arm(args, rank, world, local_rank):
     host_in.copy_(inputs)
     host_q = torch.empty(NI, *qbuf.shape[1:], dtype=torch.bfloat16, pin_memory=True)
     host_q.copy_(qbuf)
-    dev_in = torch.empty_like(inputs[0])
-    dev_q = torch.empty_like(qbuf[0])
-    host_out = torch.empty(outbuf.shape, dtype=torch.bfloat16, pin_memory=True)
+    # double-buffered: step s+1's inputs go up and step s-1's outputs come back on a copy stream while
+    # step s computes; every copy is inside the timed region
+    dev_in = [torch.empty_like(inputs[0]) for _ in range(2)]
+    dev_q = [torch.empty_like(qbuf[0]) for _ in range(2)]
+    dev_out = [torch.empty_like(outbuf) for _ in range(2)]
+    host_out = [torch.empty(outbuf.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
     e_steps = max(1, min(args.steps, 64))
+    main = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready, in_free, out_ready, out_free = ([ev(), ev()] for _ in range(4))
     barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
+    cs.wait_stream(main)
+
+    def upload(s_, j):
+        with torch.cuda.stream(cs):
+            dev_in[j].copy_(host_in[s_ % NI], non_blocking=True)
+            dev_q[j].copy_(host_q[s_ % NI], non_blocking=True)
+            in_ready[j].record(cs)
+
+    upload(0, 0)
     for s in range(e_steps):
-        dev_in.copy_(host_in[s % NI], non_blocking=True)
-        dev_q.copy_(host_q[s % NI], non_blocking=True)
-        step(s, dev_in, dev_q)
+        i = s % 2
+        if s + 1 < e_steps:
+            if s >= 1:
+                cs.wait_event(in_free[1 - i])  # step s-1 has read that buffer
+            upload(s + 1, 1 - i)
+        main.wait_event(in_ready[i])
+        if s >= 2:
+            main.wait_event(out_free[i])  # step s-2's outputs are on the host
+        step(s, dev_in[i], dev_q[i])
+        in_free[i].record(main)
         for l in range(Ly):
-            outbuf[l].copy_(outs[l])
-        host_out.copy_(outbuf, non_blocking=True)
+            dev_out[i][l].copy_(outs[l])
+        out_ready[i].record(main)
+        with torch.cuda.stream(cs):
+            cs.wait_event(out_ready[i])
+            host_out[i].copy_(dev_out[i], non_blocking=True)
+            out_free[i].record(cs)
+    main.wait_stream(cs)
     e3.record()
     torch.cuda.synchronize()
     barrier()
@@ -435,7 +463,7 @@ def gpu_arm(args, rank, world, local_rank):
             traffic = None
 
     cache_gb = cache.block_pool_k.numel() * 4 / 1e9
-    h2d_step = int((inputs[0][..., Hq:].numel() + qbuf[0].numel()) * 2)
+    h2d_step = int((inputs[0].numel() + qbuf[0].numel()) * 2)  # the bytes the e2e loop uploads per step
     d2h_step = int(outbuf.numel() * 2)
     prefill = None
     if world == 1 and args.workload == "decode" and not args.no_prefill and not args.small:
