@@ -77,16 +77,21 @@ WGKV_DEV void load_keys(const wgkv_pool& P, const int32_t* grow, int k0, int gle
 // S tile (16 rows x 64 keys) of one warp, rounded as bf16(bf16(q . k) * scale)
 template <int D>
 WGKV_DEV void score_tile(const uint32_t (&qa)[D / 16][4], const uint16_t* ks, float scale, float (&s)[8][4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+  // B fragments of two 8-key n-tiles per ldmatrix.x4: lanes 0-15 address the first tile's keys
+  // (columns kk*16 and kk*16 + 8), lanes 16-31 the second's; rows are D + 8 elements apart
+  const uint32_t base = smem_u32(ks) + uint32_t(((lane & 7) + ((lane >> 4) << 3)) * (D + 8) +
+                                                ((lane >> 3) & 1) * 8) * 2;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t* kr = reinterpret_cast<const uint32_t*>(ks + (j * 8 + g) * (D + 8));
+  for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const uint32_t b0 = kr[(kk * 16 + 2 * t4) / 2], b1 = kr[(kk * 16 + 8 + 2 * t4) / 2];
-      mma_bf16_16816(s[j], qa[kk], b0, b1);
+    for (int jp = 0; jp < 4; ++jp) {
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(b0, b1, b2, b3, base + uint32_t((jp * 16 * (D + 8) + kk * 16) * 2));
+      mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
+      mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
     }
   }
 #pragma unroll
