@@ -8,7 +8,12 @@
 // kernel with no host synchronisation: counts are reduced per 2048-token
 // chunk with warp ballots, scanned on the device, and pages are handed out by
 // a device-side bump allocator in the reference's (layer, batch, head) order
-// so the page tables come out identical.
+// so the page tables come out identical.  Also here: the QUEST page key
+// bounds kept by compaction and promotion (:744-761, :1333-1347), promotion
+// drawing on the SnapKV free list first (:694-709), the decode prologue fused
+// in front of the gate (q/k norm + RoPE, modeling_llama.py:265-271,
+// modeling_qwen3.py:236-239) and the device copy of the ring position that
+// lets a decode step replay as a CUDA graph.
 #include "common.cuh"
 #include "runtime.h"
 #include "scan.cuh"
@@ -37,7 +42,6 @@ struct GateParams {
   int64_t msb, msh, mst;
 };
 
-WGKV_DEV uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 
 WGKV_DEV float act_fn(float x, int act) {
   if (act == 1) return x / (1.f + expf(-x));             // nn.SiLU

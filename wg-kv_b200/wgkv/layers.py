@@ -7,7 +7,10 @@ Mirrors the operator surface the patched Llama/Qwen3 attention layers call
   input_shape, query_states, pre_key, key_states, value_states)`` (:1534)
 * ``self_attn_forward_patch_inference`` (:1452), ``prefill_wrapper`` (:1183),
   ``decode_wrapper`` (:1379), ``migrate_local_kv_to_global`` (:674),
-  ``refresh_local_is_global`` (:1169)
+  ``refresh_local_is_global`` (:1169), ``quest_select_blocks`` (:452),
+  ``snapkv_record_queries`` / ``snapkv_evict`` (:579, :595)
+* ``self_attn_decode_fused``: the decode step fed by raw q/k/v projection rows
+  (q/k norm + RoPE fused into the gate launch)
 
 ``self`` is the attention module (``layer_idx``, ``config``, ``head_dim``,
 ``scaling``, ``g_predictors`` and the kernel slots); ``past_key_value`` is any
@@ -15,8 +18,11 @@ attribute holder (the HF cache object), which gets the pool attributes of
 :func:`wgkv.pool.init_pool`.  Differences from the reference, all on the
 host side: batch > 1 is accepted (the pool has a batch axis); no step
 synchronises the host (page allocation, compaction and the decode schedule
-run on the device); capacity violations are reported through the device
-error word (``wgkv.check_errors()``), not an immediate assert.
+run on the device; SnapKV keeps the reference's one host read of the cached
+total to decide on eviction); capacity violations are reported through the
+device error word (``wgkv.check_errors()``), not an immediate assert.  With
+``past_key_value.wgkv_device_ring`` set the ring position is read on the
+device, so a whole decode step can be captured (``wgkv.DecodeGraph``).
 """
 from __future__ import annotations
 
