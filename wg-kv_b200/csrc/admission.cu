@@ -275,9 +275,9 @@ __global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs 
     nr += (t < L && t >= ring_start) ? 1 : 0;
   }
   int tot;
-  const int gbase = block_excl_scan(ng, wsum, tot);
+  const int gbase = block_excl_scan<kScanThreads>(ng, wsum, tot);
   int rtot;
-  const int rbase = block_excl_scan(nr, wsum, rtot);
+  const int rbase = block_excl_scan<kScanThreads>(nr, wsum, rtot);
   const int chunk_off = (c < nch) ? counts[bh * nch + c] : 0;
   const int64_t gdst0 = int64_t(first[bh]) * P.page + chunk_off;
   int gi = gbase, ri = rbase;

@@ -161,6 +161,29 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Exclusive block-wide prefix sum of one int per thread of a kThreads-thread block (warp shuffles,
+// then the warp totals); the block total comes back in `total`.  Every thread must call it; wsum
+// holds kThreads / 32 ints of shared memory and is free again on return.
+template <int kThreads>
+WGKV_DEV int block_excl_scan(int v, int* wsum, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffff, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int base = 0;
+  total = 0;
+  for (int w = 0; w < kThreads / 32; ++w) {
+    if (w < warp) base += wsum[w];
+    total += wsum[w];
+  }
+  __syncthreads();
+  return base + x - v;
+}
+
 WGKV_DEV void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }

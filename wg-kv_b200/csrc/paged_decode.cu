@@ -62,7 +62,7 @@ template <int D, int S>
 size_t smem_bytes(int BH, int G) {
   size_t s = 1024;  // alignment slack
   s += size_t(Cfg<D, S>::kStages) * Cfg<D, S>::kStageBytes;
-  s += size_t(BH + 1 + kThreads + 64) * 4;              // prefix + scan scratch
+  s += size_t(BH + 1 + kThreads) * 4;                   // prefix + scan scratch
   s += size_t(kNCW) * G * (D + 2) * 4;                  // cross-warp merge
   s += 2 * Cfg<D, S>::kStages * 8 + 64;                 // barriers + flags
   return s;
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stage_base = smem;
   int* pre = reinterpret_cast<int*>(smem + C::kStages * C::kStageBytes);
   int* scan = pre + p.BH + 1;  // kThreads ints
-  float* merge = reinterpret_cast<float*>(scan + kThreads + 64);
+  float* merge = reinterpret_cast<float*>(scan + kThreads);
   const int G = p.G;
   uint64_t* full = reinterpret_cast<uint64_t*>(merge + kNCW * G * (D + 2) + 1);
   full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
@@ -112,27 +112,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i0 = min(BH, tid * per), i1 = min(BH, i0 + per);
     int sum = 0;
     for (int i = i0; i < i1; ++i) sum += (max(p.seqlens[i], 0) + 15) >> 4;
-    // block-wide exclusive scan of the per-thread sums (warp shuffles, then the warp totals)
-    int x = sum;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffff, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) scan[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int wt = lane < kThreads / 32 ? scan[lane] : 0;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffff, wt, o);
-        if (lane >= o) wt += y;
-      }
-      if (lane < kThreads / 32) scan[32 + lane] = wt;  // inclusive warp totals
-      if (lane == kThreads / 32 - 1) pre[BH] = wt;
-    }
-    __syncthreads();
-    scan[64 + tid] = (warp ? scan[32 + warp - 1] : 0) + x - sum;  // exclusive prefix of this thread
-    __syncthreads();
-    int run = scan[64 + tid];
+    int total;
+    int run = block_excl_scan<kThreads>(sum, scan, total);  // this thread's first unit
+    if (tid == 0) pre[BH] = total;
     for (int i = i0; i < i1; ++i) {
       pre[i] = run;
       run += (max(p.seqlens[i], 0) + 15) >> 4;

@@ -24,25 +24,6 @@ constexpr int kQsWarps = kQsThreads / 32;
 // larger bf16 value -> larger key (negative values bit-flipped, positive ones offset by the sign bit)
 WGKV_DEV uint32_t score_key(uint16_t b) { return (b & 0x8000u) ? (~uint32_t(b) & 0xFFFFu) : (uint32_t(b) | 0x8000u); }
 
-// exclusive block scan of one int per thread; returns the block total through *total
-WGKV_DEV int block_excl_scan_qs(int v, int* wsum, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffff, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wsum[warp] = x;
-  __syncthreads();
-  int base = 0, tot = 0;
-  for (int w = 0; w < kQsWarps; ++w) {
-    if (w < warp) base += wsum[w];
-    tot += wsum[w];
-  }
-  __syncthreads();  // wsum is reused by the next scan
-  *total = tot;
-  return base + x - v;
-}
 
 struct QuestArgs {
   wgkv_pool P;
@@ -206,14 +187,14 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
       int eq = 0;
       for (int i = i0; i < i1; ++i) eq += keys[i] == kth;
       int tot;
-      int eq_rank = block_excl_scan_qs(eq, wsum, &tot);
+      int eq_rank = block_excl_scan<kQsThreads>(eq, wsum, tot);
       int cnt = 0;
       for (int i = i0, r = eq_rank; i < i1; ++i) {
         const uint32_t k = keys[i];
         cnt += k > kth || (k == kth && r < need);
         r += k == kth;
       }
-      int base = block_excl_scan_qs(cnt, wsum, &tot);
+      int base = block_excl_scan<kQsThreads>(cnt, wsum, tot);
       for (int i = i0, r = eq_rank; i < i1; ++i) {
         const uint32_t k = keys[i];
         if (k > kth || (k == kth && r < need)) orow[local_blocks + base++] = grow[i];

@@ -33,25 +33,6 @@ __global__ void __launch_bounds__(kScanThreads) chunk_count_kernel(MaskView mv, 
   }
 }
 
-// Block-wide exclusive scan of per-thread values (kScanThreads threads).
-WGKV_DEV int block_excl_scan(int v, int* wsum, int& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffff, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wsum[warp] = x;
-  __syncthreads();
-  int base = 0;
-  total = 0;
-  for (int w = 0; w < kScanThreads / 32; ++w) {
-    if (w < warp) base += wsum[w];
-    total += wsum[w];
-  }
-  __syncthreads();
-  return base + x - v;
-}
 
 }  // namespace
 }  // namespace wgkv

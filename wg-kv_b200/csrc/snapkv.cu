@@ -226,24 +226,6 @@ WGKV_DEV uint32_t float_key(float f) {  // ascending float order -> ascending un
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-WGKV_DEV int block_scan_excl(int v, int* wsum, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffff, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wsum[warp] = x;
-  __syncthreads();
-  int base = 0, tot = 0;
-  for (int w = 0; w < kSnWarps; ++w) {
-    if (w < warp) base += wsum[w];
-    tot += wsum[w];
-  }
-  __syncthreads();
-  *total = tot;
-  return base + x - v;
-}
 
 struct SelectArgs {
   wgkv_pool P;
@@ -321,10 +303,10 @@ __global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectA
     if (p < glen) k = float_key(pl[p]);
     const int is_eq = p < glen && k == kth;
     int tot_eq;
-    const int eq_rank = eq_seen + block_scan_excl(is_eq, wsum, &tot_eq);
+    const int eq_rank = eq_seen + block_excl_scan<kSnThreads>(is_eq, wsum, tot_eq);
     const int keep = p < glen && !(k < kth || (is_eq && eq_rank < need));
     int tot_keep;
-    const int dst = kept_base + block_scan_excl(keep, wsum, &tot_keep);
+    const int dst = kept_base + block_excl_scan<kSnThreads>(keep, wsum, tot_keep);
     if (keep) {
       const int64_t row = int64_t(grow[p / T]) * T + p % T;
       const uint4* kr = reinterpret_cast<const uint4*>(P.k + row * D);

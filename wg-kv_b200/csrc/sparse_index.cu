@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kScanThreads) idx_scatter_kernel(MaskView mv, 
     n += mk[j] ? 1 : 0;
   }
   int tot;
-  const int excl = block_excl_scan(n, wsum, tot);
+  const int excl = block_excl_scan<kScanThreads>(n, wsum, tot);
   const int base = counts[bh * nch + c] + excl;  // #admitted < t0
   int32_t* ci = o.ci + int64_t(bh) * o.ci_stride;
   int r = base;
