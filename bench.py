@@ -651,7 +651,7 @@ def c5_arm(args, rank, world, local_rank):
     per_layer = float(((W + glen) * D * 2 * 2).sum()) * 1.02
     resident = int(max(1, min(Ly, 150e9 // per_layer)))
     CFG["layers"] = resident
-    steps_total = args.warmup + args.steps + 8
+    steps_total = args.warmup + args.steps + 8 + 16  # + the end-to-end steps
     cache, rate, glen0 = build_state(dev, steps_total * ((Ly + resident - 1) // resident), seed=2 + 1000 * rank)
     layers = build_layers(dev, rate, seed=3 + 1000 * rank)
     g = torch.Generator(device=dev)
@@ -663,11 +663,11 @@ def c5_arm(args, rank, world, local_rank):
     wo = (torch.randn(hidden, Hq * D, generator=g, device=dev) * (Hq * D * world) ** -0.5).to(torch.bfloat16)
     y = torch.empty(B, hidden, dtype=torch.bfloat16, device=dev)
 
-    def step(s):
+    def step(s, xin=None, qin=None):
         for l in range(Ly):
             a = layers[l % resident]
-            x = inputs[s % NI, l]
-            q = qbuf[s % NI, l].transpose(1, 2)
+            x = inputs[s % NI, l] if xin is None else xin[l]
+            q = (qbuf[s % NI, l] if qin is None else qin[l]).transpose(1, 2)
             k = x[:, :, Hq:Hq + Hk].transpose(1, 2)
             v = x[:, :, Hq + Hk:Hq + 2 * Hk].transpose(1, 2)
             pk = x[:, :, Hq + 2 * Hk:].transpose(1, 2)
@@ -686,18 +686,73 @@ def c5_arm(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     clk = ClockSampler(local_rank) if rank == 0 else None
+    l0 = wgkv.lib.launches
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(args.steps):
         step(s)
     e1.record()
     torch.cuda.synchronize()
+    launches = wgkv.lib.launches - l0
     if world > 1:
         dist.barrier()
     clocks = clk.stop() if clk else None
     ms = max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
     wgkv.check_errors()
     glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
+
+    # end to end: each step's q/k/v/pre-k rows come from pinned host memory and the step's output
+    # (the last layer's all-reduced o_proj rows) goes back, double-buffered on a copy stream
+    host_in = torch.empty(NI, *inputs.shape[1:], dtype=torch.bfloat16, pin_memory=True)
+    host_in.copy_(inputs)
+    host_q = torch.empty(NI, *qbuf.shape[1:], dtype=torch.bfloat16, pin_memory=True)
+    host_q.copy_(qbuf)
+    dev_in = [torch.empty_like(inputs[0]) for _ in range(2)]
+    dev_q = [torch.empty_like(qbuf[0]) for _ in range(2)]
+    dev_y = [torch.empty_like(y) for _ in range(2)]
+    host_y = [torch.empty(y.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    e_steps = max(1, min(args.steps, 16))
+    main = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    in_ready, in_free, out_ready, out_free = ([torch.cuda.Event(), torch.cuda.Event()] for _ in range(4))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e6, e7 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e6.record()
+    cs.wait_stream(main)
+
+    def upload(s_, j):
+        with torch.cuda.stream(cs):
+            dev_in[j].copy_(host_in[s_ % NI], non_blocking=True)
+            dev_q[j].copy_(host_q[s_ % NI], non_blocking=True)
+            in_ready[j].record(cs)
+
+    upload(0, 0)
+    for s in range(e_steps):
+        i = s % 2
+        if s + 1 < e_steps:
+            if s >= 1:
+                cs.wait_event(in_free[1 - i])
+            upload(s + 1, 1 - i)
+        main.wait_event(in_ready[i])
+        if s >= 2:
+            main.wait_event(out_free[i])
+        step(s, dev_in[i], dev_q[i])
+        in_free[i].record(main)
+        dev_y[i].copy_(y)
+        out_ready[i].record(main)
+        with torch.cuda.stream(cs):
+            cs.wait_event(out_ready[i])
+            host_y[i].copy_(dev_y[i], non_blocking=True)
+            out_free[i].record(cs)
+    main.wait_stream(cs)
+    e7.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e = B * e_steps / (max_over_ranks(e6.elapsed_time(e7), dev) / 1e3)
+    wgkv.check_errors()
     # per-GPU attention bytes per step (32 layer visits over the resident pools)
     sl = W + (glen_start + glen_end) / 2.0
     visits = np.bincount(np.arange(Ly) % resident, minlength=resident)
@@ -730,6 +785,9 @@ def c5_arm(args, rank, world, local_rank):
                                     f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
                            "parallelism": f"tp{world} (KV heads)", **C5_CFG},
                 "per_gpu_tok_s": B / (ms / 1e3) / world,
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int((inputs[0].numel() + qbuf[0].numel()) * 2),
+                        "d2h_bytes_per_step": int(y.numel() * 2)},
+                "gpu_launches": launches,
                 "attn_hbm_gbs_per_gpu": attn_bytes / (ms / 1e3) / 1e9,
                 "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": ach, "peak": peak,
                              "peak_kind": peak_kind, "unit": "GB/s", "frac": ach / peak, "ms_per_launch": kms,
