@@ -91,7 +91,7 @@ def test_quest_golden_pipeline():
     assert np.array_equal(mn, z["final_quest_min"]) and np.array_equal(mx, z["final_quest_max"])
 
 
-@pytest.mark.parametrize("budget", [64 + 400, 64 + 17, 64 + 16 * 500])
+@pytest.mark.parametrize("budget", [64 + 400, 64 + 17, 64 + 16 * 500, 32])
 def test_quest_select_batched_matches_oracle(budget):
     import wgkv
     B, Hk, G, D, W, T, L = 2, 4, 4, 128, 64, 16, 3000
