@@ -1,6 +1,6 @@
 """Benchmark of the WG-KV admission hot path on B200.
 
-Default workload: Llama-3.1-8B-shaped decode, 32 layers,
+Default workload (C2): Llama-3.1-8B-shaped decode, 32 layers,
 batch 16, 128K-token context per sequence, 32 query / 8 KV heads, d=128,
 bf16, a 4096-token local ring, page size 16, per-(layer, sequence, head)
 global lengths from admit rates ~ Beta(2, 8).  One step = one decode token
@@ -38,7 +38,7 @@ sys.path.insert(0, os.path.join(HERE, "wg-kv_b200"))
 CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=16, ctx=131072, q_heads=32, kv_heads=8, head_dim=128,
            window=4096, page=16, admit="Beta(2,8)", gate="pre_k->64->1 GELU sigmoid", threshold=0.5)
 METRIC = "decode tok/s @128K ragged cache (Llama-8B shape, B=16, 32 layers)"
-# Qwen3-4B-shaped decode, batch 64, per-sequence context uniform in 8K..32K,
+# C4: Qwen3-4B-shaped decode, batch 64, per-sequence context uniform in 8K..32K,
 # ring 2048, aggressive gating (per-head admit ~ Beta(1,10))
 QWEN3_CFG = dict(model="Qwen3-4B-shaped", layers=36, batch=64, ctx=32768, ctx_min=8192, q_heads=32, kv_heads=8,
                  head_dim=128, window=2048, page=16, admit="Beta(1,10)", gate="pre_k->64->1 GELU sigmoid",
@@ -467,7 +467,7 @@ def gpu_arm(args, rank, world, local_rank):
     d2h_step = int(outbuf.numel() * 2)
     prefill = None
     if world == 1 and args.workload == "decode" and not args.no_prefill and not args.small:
-        # the 400K sparse prefill on the same GPU, decode cache released first
+        # the 400K sparse prefill (C3) on the same GPU, decode cache released first
         del cache, layers, inputs, qbuf, outbuf, outs, host_in, host_q, dev_in, dev_q, host_out
         torch.cuda.empty_cache()
         pl = prefill_arm(args, rank, world, local_rank, emit=False)
@@ -503,7 +503,7 @@ def gpu_arm(args, rank, world, local_rank):
 
 
 # ----------------------------------------------------------------------------
-# prefill workload: 400K tokens, 32 layers, ~30 % admitted
+# prefill workload (C3): 400K tokens, 32 layers, ~30 % admitted
 # ----------------------------------------------------------------------------
 PCFG = dict(model="Llama-3.1-8B-shaped", layers=32, seq_len=400000, q_heads=32, kv_heads=8, head_dim=128,
             window=4096, page=16, admit="~30% mean per head", max_tokens_per_head=401000,
@@ -626,7 +626,7 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
 
 
 # ----------------------------------------------------------------------------
-# Llama-8B decode, batch 64 at 256K context, KV heads sharded across GPUs
+# C5: Llama-8B decode, batch 64 at 256K context, KV heads sharded across GPUs
 # (8 -> 8/N per GPU, each GPU its own paged pool), row-parallel o_proj + NCCL all-reduce per layer.
 # ----------------------------------------------------------------------------
 C5_CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=64, ctx=262144, q_heads=32, kv_heads=8, head_dim=128,
