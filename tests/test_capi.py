@@ -36,9 +36,10 @@ def test_every_entry_point_the_host_layer_calls_is_declared_and_exported():
     import glob
     import os
     import re
+    import wgkv
     from wgkv._lib import LIB_PATH, parse_header
-    pkg = os.path.dirname(LIB_PATH)
-    repo = os.path.dirname(os.path.dirname(pkg))
+    pkg = os.path.dirname(os.path.abspath(wgkv.__file__))
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     used = set()
     for f in (glob.glob(os.path.join(pkg, "*.py")) + glob.glob(os.path.join(repo, "tests", "*.py")) +
               [os.path.join(repo, "bench.py"), os.path.join(repo, "__graft_entry__.py")]):
