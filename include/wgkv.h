@@ -59,6 +59,14 @@ extern "C" {
 #define WGKV_ERR_BAD_PAGE 0x8       /* a page id outside [0, total_blocks) was met */
 #define WGKV_ERR_BAD_POSITION 0x10  /* a RoPE position outside the caller's tables (clamped) */
 
+/*
+ * Failure-path self test (no reference counterpart): one CTA waits on an mbarrier that nothing ever
+ * completes, with the bounded wait every pipelined kernel here uses; after the limit (about two
+ * seconds) it ORs WGKV_ERR_TIMEOUT into *err and returns.  No fault, no trap: the context stays
+ * usable, which is what the tests of the error path check.
+ */
+WGKV_API int wgkv_selftest_wait_limit(int* err, void* stream);
+
 /* Library version and build info. */
 WGKV_API int wgkv_version(void);
 /* Number of SMs of the current device (cached per device). <0 on error. */
