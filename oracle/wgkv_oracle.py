@@ -11,7 +11,10 @@ Parity pin: the restatement is checked against golden vectors that
 code (``src/modeling_layers.py`` imported unmodified, on CPU) and the
 reference's own test oracles (``utils/test_flash_attn_with_kvcache.py:16-71``,
 ``utils/test_sparse_attn.py:34-93``).  ``tests/test_oracle_golden.py`` does the
-check.
+check -- including QUEST page selection (``quest_select_blocks`` :452-576) and
+SnapKV eviction (``snapkv_evict`` :595-671), whose fixtures record what the
+reference selected / evicted (equal up to the order of tied scores, which
+``torch.topk`` leaves unspecified; the restatement takes the lower positions).
 
 Layout conventions (batch generalisation of the reference, identical to it
 for batch 1):
