@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
 Run where a checkout of the reference is available (its location in the
-``WGKV_REFERENCE`` environment variable, or the default below).  The reference's
+``WGKV_REFERENCE`` environment variable, required).  The reference's
 ``src/modeling_layers.py`` is imported unmodified and driven on CPU:
 
 * ``GatingPredictor`` fast path (``:170-196``) -> admission scores / mask
@@ -34,7 +34,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import wgkv_oracle as O  # noqa: E402
 
-REF = os.environ.get("WGKV_REFERENCE", "/root/reference")
+REF = os.environ.get("WGKV_REFERENCE")
+if not REF and __name__ == "__main__":
+    sys.exit("set WGKV_REFERENCE to the root of an unmodified WG-KV checkout (the directory holding src/ and utils/)")
 
 
 def load_reference():

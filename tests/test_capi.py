@@ -50,3 +50,20 @@ def test_every_entry_point_the_host_layer_calls_is_declared_and_exported():
     lib = ctypes.CDLL(LIB_PATH)
     missing = [n for n in used if not hasattr(lib, n)]
     assert not missing, missing
+
+
+def test_decode_argument_checks_run_before_any_device_work():
+    """Both decode entry points refuse an unsupported head_dim with WGKV_EINVAL before they enqueue
+    anything, so the check needs no GPU (the pointers are never dereferenced)."""
+    if not os.path.exists(LIB_PATH):
+        pytest.skip("libwgkv.so not built")
+    from wgkv import lib
+    fake = 4096  # non-null, 16-byte aligned, never touched
+    for hd in (96, 32, 256):
+        assert lib.wgkv_paged_decode_noalloc(fake, fake, fake, 8, 16, fake, fake, 1, 1, 8, 2, hd, 1.0, fake, fake,
+                                             None) == -1
+        assert lib.wgkv_paged_decode(fake, fake, fake, 8, 16, fake, fake, 1, 1, 8, 2, hd, 1.0, fake, fake, 1 << 20,
+                                     fake, None) == -1
+    # a missing output is refused before the size check of the static scratch
+    assert lib.wgkv_paged_decode_noalloc(fake, fake, fake, 8, 16, fake, fake, 1, 4096, 128, 8, 128, 1.0, None, fake,
+                                         None) == -1

@@ -115,3 +115,25 @@ def test_triton_handle_signature(wgkv):
     with pytest.raises(TypeError):
         wgkv.flash_attn_with_kvcache_wrapper_triton_handle(to_bf16(q).half(), to_bf16(kc), to_bf16(vc),
                                                            torch.from_numpy(sl).cuda(), torch.from_numpy(tbl).cuda(), 1.0)
+
+
+def test_workspace_counter_prefix_grows(wgkv):
+    """A second call with more (batch, kv-head) counters than the first reuses the cached workspace:
+    the counter bytes it adds held the first call's partial results and must be cleared."""
+    small = make_case(31, 1, 32, 2, 128, 16, 30000, garbage=False)   # few counters, large partials
+    large = make_case(32, 20, 8, 8, 64, 16, 700, garbage=False)      # 160 counters, small partials
+    for q, kc, vc, sl, tbl in (small, large, small, large):
+        D = q.shape[-1]
+        o = run(wgkv, q, kc, vc, sl, tbl, D ** -0.5)
+        np.testing.assert_allclose(o, O.paged_decode(q, kc, vc, sl, tbl, D ** -0.5), atol=ATOL, rtol=RTOL)
+
+
+def test_argmax_ticket_prefix_grows():
+    """Same rule for the argmax tickets: one long row, then many short rows, on one stream."""
+    from wgkv.model import argmax_into
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for rows, n in ((1, 128256), (100, 1000), (1, 128256), (100, 1000)):
+        x = torch.randn(rows, n, device="cuda", generator=g)
+        out = torch.empty(rows, 1, dtype=torch.int64, device="cuda")
+        argmax_into(x, out)
+        assert torch.equal(out, x.argmax(-1, keepdim=True))

@@ -82,3 +82,14 @@ def test_noalloc_rejects_oversize():
     out = torch.empty_like(q)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     assert _call_noalloc(lib, q, kc, kc, sl, tbl, out, err, 1.0) == -3  # WGKV_ENOSPC
+
+
+def test_noalloc_refuses_bad_head_dim_before_touching_the_array():
+    from wgkv._lib import lib
+    q = torch.zeros(1, 1, 8, 96, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(4, 16, 96, dtype=torch.bfloat16, device="cuda")
+    sl = torch.ones(1, 2, dtype=torch.int32, device="cuda")
+    tbl = torch.zeros(1, 2, 1, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert _call_noalloc(lib, q, kc, kc, sl, tbl, out, err, 1.0) == -1  # WGKV_EINVAL, not ENOSPC

@@ -16,9 +16,28 @@
 // lets a decode step replay as a CUDA graph.
 #include "common.cuh"
 #include "runtime.h"
-#include "scan.cuh"
 
 namespace wgkv {
+
+// Mask counting per 2048-token chunk (declared in common.cuh; also launched by the sparse-index builder).
+__global__ void __launch_bounds__(kScanThreads) chunk_count_kernel(MaskView mv, int Hk, int limit, int nch,
+                                                                   int* counts) {
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk, c = blockIdx.x;
+  const int t0 = c * kChunk + threadIdx.x * 8;
+  int n = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) n += (t0 + j < limit) && mv.at(b, h, t0 + j) ? 1 : 0;
+  for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xffffffff, n, o);
+  __shared__ int wsum[kScanThreads / 32];
+  if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < kScanThreads / 32; ++w) s += wsum[w];
+    counts[bh * nch + c] = s;
+  }
+}
+
 namespace {
 
 // ============================================================================

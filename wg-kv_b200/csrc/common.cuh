@@ -200,4 +200,18 @@ WGKV_DEV void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }
 
+// ---- chunked mask counting shared by the compaction kernels (admission, sparse indices) ----
+constexpr int kChunk = 2048;       // tokens per counting / scatter CTA
+constexpr int kScanThreads = 256;  // 8 tokens per thread
+
+struct MaskView {
+  const uint8_t* m;
+  int64_t sb, sh, st;
+  WGKV_DEV uint8_t at(int b, int h, int t) const { return m[b * sb + h * sh + int64_t(t) * st]; }
+};
+
+// counts[bh * nch + c] = #admitted tokens of (b, h) in chunk c of [0, limit); defined in admission.cu,
+// launched there and by the sparse-index builder.
+__global__ void chunk_count_kernel(MaskView mv, int Hk, int limit, int nch, int* counts);
+
 }  // namespace wgkv

@@ -195,6 +195,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       rs = re;
     }
+    // Leave only once every load this warp issued has landed: if a consumer gave up waiting
+    // (WGKV_ERR_TIMEOUT) the CTA may otherwise retire with bulk copies still writing its shared
+    // memory.  On the normal path these phases completed long ago and each wait returns at once.
+    if (lane == 0) {
+      for (int j = max(0, it - C::kStages); j < it; ++j) {
+        if (!mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1)) set_error(p.err, WGKV_ERR_TIMEOUT);
+      }
+    }
     return;
   }
 
@@ -504,6 +512,19 @@ int launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t nu
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
+// Argument checks shared by both decode entry points (run before anything is enqueued).
+int check_decode_args(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t num_pages,
+                      int page_size, const int32_t* cache_seqlens, const int32_t* block_table, int batch,
+                      int num_q_heads, int num_kv_heads, int head_dim, const uint16_t* out) {
+  if (!q || !k_cache || !v_cache || !cache_seqlens || !block_table || !out) return WGKV_EINVAL;
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
+  if (num_q_heads / num_kv_heads > 16 || page_size <= 0 || page_size % 16 != 0 || num_pages <= 0) return WGKV_EINVAL;
+  if (head_dim != 64 && head_dim != 128) return WGKV_EINVAL;
+  if (batch * num_kv_heads > kMaxBH) return WGKV_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return WGKV_EINVAL;
+  return WGKV_OK;
+}
+
 }  // namespace
 }  // namespace wgkv
 
@@ -521,11 +542,10 @@ extern "C" int wgkv_paged_decode(const uint16_t* q, const uint16_t* k_cache, con
                                  int num_kv_heads, int head_dim, float softmax_scale, uint16_t* out, void* workspace,
                                  size_t workspace_bytes, int* err, void* stream) {
   using namespace wgkv;
-  if (!q || !k_cache || !v_cache || !cache_seqlens || !block_table || !out || !workspace) return WGKV_EINVAL;
-  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
-  if (num_q_heads / num_kv_heads > 16 || page_size <= 0 || page_size % 16 != 0 || num_pages <= 0) return WGKV_EINVAL;
-  if (batch * num_kv_heads > kMaxBH) return WGKV_EINVAL;
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return WGKV_EINVAL;
+  if (!workspace) return WGKV_EINVAL;
+  const int chk = check_decode_args(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table, batch,
+                                    num_q_heads, num_kv_heads, head_dim, out);
+  if (chk != WGKV_OK) return chk;
   constexpr size_t kMaxSmem = 227 * 1024;
   const int BH = batch * num_kv_heads, G = num_q_heads / num_kv_heads;
   const cudaStream_t st = as_stream(stream);
@@ -576,7 +596,9 @@ extern "C" int wgkv_paged_decode_noalloc(const uint16_t* q, const uint16_t* k_ca
                                          const int32_t* block_table, int64_t table_stride, int batch,
                                          int num_q_heads, int num_kv_heads, int head_dim, float softmax_scale,
                                          uint16_t* out, int* err, void* stream) {
-  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return WGKV_EINVAL;
+  const int chk = wgkv::check_decode_args(q, k_cache, v_cache, num_pages, page_size, cache_seqlens, block_table,
+                                          batch, num_q_heads, num_kv_heads, head_dim, out);
+  if (chk != WGKV_OK) return chk;
   const size_t need = wgkv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim);
   if (need > WGKV_PAGED_DECODE_STATIC_SCRATCH_BYTES) return WGKV_ENOSPC;
   int dev = 0;

@@ -8,7 +8,6 @@
 // and Gmax is reduced with an atomicMax into a device word.
 #include "common.cuh"
 #include "runtime.h"
-#include "scan.cuh"
 
 namespace wgkv {
 namespace {

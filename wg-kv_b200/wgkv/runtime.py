@@ -1,7 +1,11 @@
 """Per-device state shared by the ops: error word, scratch workspaces, streams.
 
 Workspaces are cached per (device, stream, purpose) and only grow.  Their
-leading counters are zeroed once at allocation; the kernels leave them zero.
+leading counters must be zero when a kernel starts and the kernels leave them
+zero; a cached buffer records how many leading bytes are known to be zero, and
+a call that needs a longer counter prefix (more heads, more rows) zeroes the
+extra bytes first, since they may hold an earlier call's partial results.
+After a call only its own prefix is known to be zero.
 """
 from __future__ import annotations
 
@@ -51,12 +55,17 @@ def check_errors(device=None, reset: bool = True):
 def workspace(device, purpose: str, nbytes: int, zero_prefix: int = 0) -> torch.Tensor:
     d = torch.device(device)
     key = (d.index, torch.cuda.current_stream(d).cuda_stream, purpose)
-    ws = _workspaces.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=d)
-        if zero_prefix:
-            ws[:zero_prefix].zero_()
-        _workspaces[key] = ws
+    ent = _workspaces.get(key)
+    if ent is None or ent[0].numel() < nbytes:
+        ws = torch.empty(max(nbytes, zero_prefix, 256), dtype=torch.uint8, device=d)
+        zeroed = 0
+    else:
+        ws, zeroed = ent
+    if zero_prefix > zeroed:
+        # stream-ordered: runs after every earlier user of this buffer on this stream
+        ws[zeroed:zero_prefix].zero_()
+    # this call's kernels may write anything past its own prefix and leave the prefix zero
+    _workspaces[key] = (ws, zero_prefix)
     return ws
 
 
