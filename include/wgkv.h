@@ -126,15 +126,23 @@ typedef struct wgkv_pool {
 /* insert_pos / local_ptr value that means "read the position from pool->ring_state". */
 #define WGKV_RING_ON_DEVICE (-1)
 
+/* `act` flag of the gate entry points: GatingPredictor's conv path (g_fast_path=False). */
+#define WGKV_GATE_SILU 0x1
+#define WGKV_GATE_CONV 0x2
+
 /* ---- (a1, a2) write gate + admission mask --------------------------------- */
 /*
  * scores[b,h,t] = bf16(sigmoid(w2_h . act(W1_h x + b1_h) + b2_h)), mask = scores > threshold,
  * x = concat of the inputs selected by `input_mask` (bit 0 pre_k, bit 1 post_k, bit 2 value, in that
  * order), each optionally RMS-normalised with its row of `norm_w` (3, D) when norm_w != NULL.  Rounds
- * to bf16 where the reference's bf16 tensors do (GatingPredictor fast path, :170-196); GEMM
- * accumulation is fp32.  Inputs are (B, Hk, L, D) with element strides (sb, sh, st); unused inputs
- * may be NULL.  w1 (Hk, inner, I), b1 (Hk, inner), w2 (Hk, inner), b2 (Hk) bf16.  Either output may
- * be NULL; strides are in elements.  act: 0 GELU (erf), 1 SiLU.
+ * to bf16 where the reference's bf16 tensors do; GEMM accumulation is fp32.  `act` bit 0 picks the
+ * activation (0 GELU (erf), 1 SiLU); bit 1 (WGKV_GATE_CONV) picks the reference's default
+ * g_fast_path=False numerics (:198-205: each 1x1 conv rounds once, after its bias, and the score is
+ * floored at bf16(score_floor) = g_epsilon by torch.clamp before the threshold); without it the
+ * einsum fast path (:185-196: products rounded, then the bias added and rounded; score_floor unused).
+ * Inputs are (B, Hk, L, D) with element strides (sb, sh, st); unused inputs may be NULL.  w1
+ * (Hk, inner, I), b1 (Hk, inner), w2 (Hk, inner), b2 (Hk) bf16.  Either output may be NULL; strides
+ * are in elements.
  * Constraints: D in {64, 128}; inner % 8 == 0; I = D * popcount(input_mask) <= 384.
  */
 WGKV_API int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
@@ -142,8 +150,8 @@ WGKV_API int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_s
                               const uint16_t* value, int64_t v_sb, int64_t v_sh, int64_t v_st, int batch,
                               int kv_heads, int seq_len, int head_dim, int input_mask, const uint16_t* w1,
                               const uint16_t* b1, const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w,
-                              float rms_eps, int inner, int act, float threshold, uint16_t* scores, int64_t s_sb,
-                              int64_t s_sh, int64_t s_st, uint8_t* mask, int64_t m_sb, int64_t m_sh, int64_t m_st,
+                              float rms_eps, int inner, int act, float score_floor, float threshold,
+                              uint16_t* scores, int64_t s_sb, int64_t s_sh, int64_t s_st, uint8_t* mask, int64_t m_sb, int64_t m_sh, int64_t m_st,
                               void* stream);
 
 /* ---- (a3) prefill: ring fill + admission compaction ----------------------- */
@@ -196,7 +204,7 @@ WGKV_API int wgkv_decode_append(const wgkv_pool* pool, int layer, int insert_pos
 
 /*
  * Decode step without deferred gating, fused: the write gate on the new token of every (b, h)
- * (same MLP, inputs and rounding as wgkv_gate_scores) writes its admission bit into ring slot
+ * (same MLP, inputs, `act` flags, floor and rounding as wgkv_gate_scores) writes its admission bit into ring slot
  * `insert_pos` of local_is_global, k_new / v_new go into that ring slot, and cache_seqlens is
  * filled as in wgkv_decode_append -- one launch (reference: the gate call in
  * self_attn_forward_patch :1579 + decode_wrapper :1390-1400, :1429-1432).  Gate inputs are the
@@ -209,7 +217,7 @@ WGKV_API int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int inser
                                      int64_t k_sb, int64_t k_sh, const uint16_t* v_new, int64_t v_sb, int64_t v_sh,
                                      int input_mask, const uint16_t* w1, const uint16_t* b1, const uint16_t* w2,
                                      const uint16_t* b2, const uint16_t* norm_w, float rms_eps, int inner, int act,
-                                     float threshold, int32_t* cache_seqlens, void* stream);
+                                     float score_floor, float threshold, int32_t* cache_seqlens, void* stream);
 
 /*
  * Decode prologue fused into the above (the q/k/v projection epilogue of the patched attention
@@ -229,7 +237,8 @@ WGKV_API int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_p
                                   const uint16_t* rope_sin, const int64_t* position, int64_t n_positions,
                                   uint16_t* q_out, int input_mask, const uint16_t* w1, const uint16_t* b1,
                                   const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
-                                  int inner, int act, float threshold, int32_t* cache_seqlens, void* stream);
+                                  int inner, int act, float score_floor, float threshold, int32_t* cache_seqlens,
+                                  void* stream);
 
 /* ---- QUEST block selection (use_quest) ------------------------------------ */
 /*

@@ -97,6 +97,8 @@ class GateParams:
     rms: bool = False
     rms_eps: float = 1e-6
     norms: dict = field(default_factory=dict)
+    fast_path: bool = True   # g_fast_path (configuration_llama.py:207 defaults to False)
+    epsilon: float = 0.0     # g_epsilon: score floor of the conv path (:205)
 
 
 def _rms_norm_bf16(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
@@ -116,6 +118,18 @@ def _act(x: np.ndarray, kind: str) -> np.ndarray:
     return bf16(y.astype(np.float32))
 
 
+def _gate_states(p: GateParams, pre_key, post_key, value) -> np.ndarray:
+    """Concatenation of the selected (optionally RMS-normed) inputs, modeling_layers.py:172-183."""
+    src = {"pre_k": pre_key, "post_k": post_key, "v": value}
+    parts = []
+    for name in p.inputs:
+        x = src[name].astype(np.float32)
+        if p.rms:
+            x = _rms_norm_bf16(x, p.norms[name], p.rms_eps)
+        parts.append(x)
+    return np.concatenate(parts, axis=-1)  # (B, Hk, L, I)
+
+
 def gate_logits_nobias(p: GateParams, pre_key=None, post_key=None, value=None) -> np.ndarray:
     """``einsum(act(einsum(x, w1) + b1), w2)`` rounded to bf16, before ``+ b2``.
 
@@ -124,14 +138,7 @@ def gate_logits_nobias(p: GateParams, pre_key=None, post_key=None, value=None) -
     rounded to bf16, ``+ b1`` (bf16), activation (bf16), einsum with w2
     (bf16).  Inputs are ``(B, Hk, L, D)``; returns ``(B, Hk, L)``.
     """
-    src = {"pre_k": pre_key, "post_k": post_key, "v": value}
-    parts = []
-    for name in p.inputs:
-        x = src[name].astype(np.float32)
-        if p.rms:
-            x = _rms_norm_bf16(x, p.norms[name], p.rms_eps)
-        parts.append(x)
-    states = np.concatenate(parts, axis=-1)  # (B, Hk, L, I)
+    states = _gate_states(p, pre_key, post_key, value)
     h = np.matmul(states, np.swapaxes(p.w1.astype(np.float32), -1, -2)[None])
     h = bf16(h)
     h = bf16(h + p.b1[None, :, None, :])
@@ -147,10 +154,28 @@ def gate_finish(o: np.ndarray, b2: np.ndarray) -> np.ndarray:
     return bf16(s.astype(np.float32))
 
 
+def gate_scores_conv(p: GateParams, pre_key=None, post_key=None, value=None) -> np.ndarray:
+    """The reference's default gate path (``g_fast_path=False``, modeling_layers.py:198-205):
+    grouped 1x1 ``conv1`` (fp32 accumulation with the bias, one bf16 rounding), activation (bf16),
+    ``conv2`` (fp32 accumulation with the bias, one rounding), sigmoid (bf16), then
+    ``torch.clamp(min=g_epsilon)``, whose floor is ``g_epsilon`` rounded to bf16."""
+    states = _gate_states(p, pre_key, post_key, value)
+    h = np.matmul(states, np.swapaxes(p.w1.astype(np.float32), -1, -2)[None])
+    h = bf16((h + p.b1[None, :, None, :]).astype(np.float32))
+    h = _act(h, p.act)
+    o = np.matmul(h, p.w2.astype(np.float32)[None, :, :, None])[..., 0]
+    o = bf16((o + p.b2[None, :, None]).astype(np.float32))
+    s = bf16((1.0 / (1.0 + np.exp(-o.astype(np.float64)))).astype(np.float32))
+    floor = bf16(np.float32(p.epsilon))
+    return np.where(s < floor, floor, s).astype(np.float32)
+
+
 def gate_scores(p: GateParams, pre_key=None, post_key=None, value=None) -> np.ndarray:
     """g = sigmoid(w2 . act(w1 . x + b1) + b2) per (b, h, t), bf16 at op boundaries
-    (GatingPredictor.forward fast path, modeling_layers.py:170-196).
-    Returns ``(B, Hk, L)`` float32 on the bf16 grid."""
+    (GatingPredictor.forward, modeling_layers.py:170-205: the einsum fast path, or the conv
+    path when ``p.fast_path`` is False).  Returns ``(B, Hk, L)`` float32 on the bf16 grid."""
+    if not p.fast_path:
+        return gate_scores_conv(p, pre_key, post_key, value)
     return gate_finish(gate_logits_nobias(p, pre_key, post_key, value), p.b2)
 
 

@@ -442,9 +442,44 @@ def gate_checkpoint_case(m):
     print("gate_ckpt written")
 
 
+def gate_conv_case(m):
+    """The reference's default gate path, ``g_fast_path=False`` (src/modeling_layers.py:198-205:
+    grouped conv1d, one rounding per conv, ``clamp(min=g_epsilon)``), run by the reference's own
+    GatingPredictor on seeded inputs.  Two configurations: pre_k only / GELU / expand 0.5 with a
+    floor (0.2) above some scores, and RMS pre_k + post_k + v / SiLU / expand 1.5."""
+    torch.manual_seed(11)
+    rng = np.random.default_rng(111)
+    out = {}
+    cfgs = [("a", 128, 8, 256, ["pre_k"], "gelu", 0.5, 0.2, False),
+            ("b", 64, 2, 300, ["pre_k", "post_k", "v"], "silu", 1.5, 1e-3, True)]
+    for name, D, Hk, L, inputs, act, expand, eps, rms in cfgs:
+        gp = m.GatingPredictor(D, Hk, inputs, act, expand, eps, rms, False)
+        with torch.no_grad():
+            # widen the score spread so both thresholds cut through the distribution
+            gp.conv2.weight.mul_(8.0)
+            if rms:
+                for norm in (gp.pre_key_norm, gp.post_key_norm, gp.value_norm):
+                    norm.weight.add_(0.1 * torch.randn(D))
+        gp = gp.to(torch.bfloat16)
+        for k_, v_ in gp.state_dict().items():
+            out[f"{name}_{k_}"] = O.bf16_bits(v_.float().numpy())
+        xs = [O.randn_bf16(rng, (1, Hk, L, D)) for _ in range(3)]
+        with torch.no_grad():
+            sc = gp(tb(xs[0]), tb(xs[1]), tb(xs[2]))
+        out[f"{name}_scores"] = O.bf16_bits(nb(sc))
+        out[f"{name}_x"] = np.stack([O.bf16_bits(x) for x in xs])
+        out[f"{name}_cfg"] = np.array([D, Hk, L, int(expand * D)], np.int64)
+        out[f"{name}_eps"] = np.float64(eps)
+    np.savez_compressed(os.path.join(HERE, "gate_conv.npz"), **out)
+    print("gate_conv written")
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 1)
     m, t = load_reference()
+    if os.environ.get("WGKV_GOLDEN_ONLY") == "gate_conv":
+        gate_conv_case(m)
+        return
     if os.environ.get("WGKV_GOLDEN_ONLY") == "gate_ckpt":
         gate_checkpoint_case(m)
         return
@@ -455,6 +490,7 @@ def main():
         quest_case(m, t)
         return
     gate_checkpoint_case(m)
+    gate_conv_case(m)
     decode_cases(t)
     indices_cases(m)
     # C1: the CPU-reference single-layer configuration (32 q / 8 kv heads,

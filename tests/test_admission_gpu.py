@@ -240,14 +240,16 @@ def test_pooled_prefill_matches_gather(wgkv, B, Hk, G, D):
     assert torch.equal(pooled, gathered)
 
 
+@pytest.mark.parametrize("fast", [True, False])
 @pytest.mark.parametrize("inputs,rms,act,inner", [(["pre_k"], False, "gelu", 64), (["pre_k", "post_k"], True, "gelu", 512),
                                                    (["post_k", "v"], False, "silu", 192)])
-def test_fused_decode_gate_matches_gate_kernel(wgkv, inputs, rms, act, inner):
-    """wgkv_decode_gate_append writes the same admission bits / ring rows as the gate kernel + append."""
+def test_fused_decode_gate_matches_gate_kernel(wgkv, inputs, rms, act, inner, fast):
+    """wgkv_decode_gate_append writes the same admission bits / ring rows as the gate kernel + append
+    (both gate numerics: the einsum fast path and the conv path with its clamp floor)."""
     from types import SimpleNamespace
     B, Hk, D, W, T = 6, 4, 128, 64, 16
     torch.manual_seed(0)
-    gp = wgkv.GatingPredictor(D, Hk, inputs, act, inner / D, 1e-3, rms, True).cuda().bfloat16()
+    gp = wgkv.GatingPredictor(D, Hk, inputs, act, inner / D, 0.45, rms, fast).cuda().bfloat16()
     if rms:
         with torch.no_grad():
             gp.pre_key_norm.weight.add_(0.1 * torch.randn_like(gp.pre_key_norm.weight))
@@ -267,3 +269,28 @@ def test_fused_decode_gate_matches_gate_kernel(wgkv, inputs, rms, act, inner):
         assert torch.equal(rows, k[:, :, 0])
         assert torch.equal(cache.cache_seqlens, torch.full((B, Hk), 7, dtype=torch.int32, device="cuda"))
     assert mism <= 1, mism  # accumulation order differs; a bit may flip only at an exact bf16 tie
+
+
+@pytest.mark.parametrize("name", ["a", "b"])
+def test_gate_conv_path_matches_reference(wgkv, name):
+    """g_fast_path=False (the reference's default, src/configuration_llama.py:207): the CUDA gate
+    reproduces the reference GatingPredictor's conv-path scores (:198-205, clamp floor included) and
+    its masks bit-exactly, at a threshold above and one below the floor."""
+    from gate_conv_util import conv_case
+    p, ins, ref, (D, Hk, L, inner), eps, z, inputs, act, rms = conv_case(name)
+    gp = wgkv.GatingPredictor(D, Hk, inputs, act, inner / D, eps, rms, False).cuda().bfloat16()
+    with torch.no_grad():
+        for k_, v_ in gp.state_dict().items():
+            v_.copy_(torch.from_numpy(O.from_bf16_bits(z[f"{name}_{k_}"])).reshape(v_.shape))
+    x = [bhld(ins[k]) for k in ("pre_key", "post_key", "value")]
+    s = gp(*x)
+    torch.cuda.synchronize()
+    got = bits(s)
+    assert int((got != O.bf16_bits(ref)).sum()) <= max(1, got.size // 2000)
+    for thr in (0.5, 0.1):
+        mask = torch.empty(s.shape, dtype=torch.uint8, device="cuda")
+        gp.admit(*x, thr, mask)
+        assert np.array_equal(to_np(mask).astype(bool), O.admission_mask(ref, thr)), thr
+    # the fast-path numerics really differ here (the flag reaches the kernel)
+    gp.g_fast_path = True
+    assert (bits(gp(*x)) != got).sum() > got.size // 20

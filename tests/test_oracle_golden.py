@@ -223,3 +223,18 @@ def test_snapkv_eviction_matches_reference():
                             O.bf16_bits(st.k), O.bf16_bits(st.v), st.page, st.window)
         assert np.array_equal(dig, z[f"d{s}_pool_sha"]), s
     assert n_ev[0] == int(z["snap_n_evictions"]) == 2
+
+
+@pytest.mark.parametrize("name", ["a", "b"])
+def test_gate_conv_path_matches_reference(name):
+    """g_fast_path=False (the reference's default): the oracle's conv-path scores equal the reference's
+    (rare 1-ulp accumulation-order differences allowed) and the masks at two thresholds, one below the
+    clamp floor, are identical."""
+    from gate_conv_util import conv_case
+    p, ins, ref, _, eps, *_ = conv_case(name)
+    s = O.gate_scores(p, **ins)
+    mism = int((O.bf16_bits(s) != O.bf16_bits(ref)).sum())
+    assert mism <= max(1, s.size // 2000), (mism, s.size)
+    assert (ref >= O.bf16(np.float32(eps))).all()
+    for thr in (0.5, 0.1):
+        assert np.array_equal(O.admission_mask(s, thr), O.admission_mask(ref, thr))

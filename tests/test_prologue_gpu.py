@@ -86,8 +86,13 @@ def test_prologue_matches_unfused(qk_norm, B, Hk, G, D):
         torch.testing.assert_close(ring(ca, ca.block_pool_k).float(), ring(cb, cb.block_pool_k).float(), atol=2e-2,
                                    rtol=1e-2)
         assert torch.equal(ring(ca, ca.block_pool_v), ring(cb, cb.block_pool_v))
-        agree = (ca.local_is_global == cb.local_is_global).float().mean().item()
-        assert agree >= 0.95, agree  # only keys within rounding of the threshold may differ
+        # Admission bits may differ only where the normalised key's last-bit differences can move the
+        # score across the threshold: the unfused score within one bf16 ulp at 0.5 (2^-8) of it.
+        s_ref = gp(pk[:, :, None], kr[:, :, None], v[:, :, None])[:, :, 0].float()
+        differ = (ca.local_is_global[layer, :, :, ins] != cb.local_is_global[layer, :, :, ins])
+        near = (s_ref - 0.5).abs() <= 2.0 ** -8
+        assert int((differ & ~near).sum()) == 0, (int(differ.sum()), int((differ & ~near).sum()))
+        assert int(differ.sum()) <= max(1, differ.numel() // 8)
     assert torch.equal(ca.cache_seqlens, cb.cache_seqlens)
 
 

@@ -14,6 +14,9 @@
 // in front of the gate (q/k norm + RoPE, modeling_llama.py:265-271,
 // modeling_qwen3.py:236-239) and the device copy of the ring position that
 // lets a decode step replay as a CUDA graph.
+#include <math.h>
+#include <string.h>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -52,9 +55,9 @@ struct GateParams {
   int64_t sb[3], sh[3], st[3];
   const uint16_t* norm[3];
   int n_in;
-  int B, Hk, L, D, I, inner, act;
+  int B, Hk, L, D, I, inner, act;  // act: WGKV_GATE_SILU | WGKV_GATE_CONV bits
   const uint16_t *w1, *b1, *w2, *b2;
-  float eps, thr;
+  float eps, thr, floor;             // floor: bf16 score floor of the conv path (-inf on the fast path)
   uint16_t* scores;
   int64_t ssb, ssh, sst;
   uint8_t* mask;
@@ -63,8 +66,22 @@ struct GateParams {
 
 
 WGKV_DEV float act_fn(float x, int act) {
-  if (act == 1) return x / (1.f + expf(-x));             // nn.SiLU
+  if (act & WGKV_GATE_SILU) return x / (1.f + expf(-x));       // nn.SiLU
   return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));  // nn.GELU() (erf form)
+}
+
+// Hidden pre-activation from the fp32 dot product: the conv path (g_fast_path=False, :198-201)
+// rounds once after the bias; the einsum fast path (:185-187) rounds the product, then the sum.
+WGKV_DEV float gate_hidden(float dot, float bias, int act) {
+  return (act & WGKV_GATE_CONV) ? bf16_round(dot + bias) : bf16_round(bf16_round(dot) + bias);
+}
+
+// Score from the fp32 output dot product: bias (same rounding rule), sigmoid in bf16, then the
+// conv path's torch.clamp(min=g_epsilon) (:205; NaN stays NaN as in torch).
+WGKV_DEV float gate_score(float dot, float bias, int act, float floor) {
+  const float o = (act & WGKV_GATE_CONV) ? bf16_round(dot + bias) : bf16_round(bf16_round(dot) + bias);
+  const float s = bf16_round(1.f / (1.f + expf(-o)));
+  return s < floor ? floor : s;
 }
 
 __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
@@ -163,8 +180,8 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
       for (int e = 0; e < 2; ++e) {
         const int n = j * 8 + 2 * t4 + e;
         const float bb = b1s[n], ww = w2s[n];
-        float h0 = bf16_round(bf16_round(acc[j][e]) + bb);
-        float h1 = bf16_round(bf16_round(acc[j][2 + e]) + bb);
+        float h0 = gate_hidden(acc[j][e], bb, p.act);
+        float h1 = gate_hidden(acc[j][2 + e], bb, p.act);
         part0 += bf16_round(act_fn(h0, p.act)) * ww;
         part1 += bf16_round(act_fn(h1, p.act)) * ww;
       }
@@ -181,9 +198,7 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
       const int gr = row0 + warp * 16 + g + rr * 8;
       if (gr >= nrows) continue;
       const int b = gr / p.L, t = gr - b * p.L;
-      float o = bf16_round(rr ? part1 : part0);
-      o = bf16_round(o + b2);
-      const float s = bf16_round(1.f / (1.f + expf(-o)));
+      const float s = gate_score(rr ? part1 : part0, b2, p.act, p.floor);
       if (p.scores) p.scores[b * p.ssb + h * p.ssh + int64_t(t) * p.sst] = f2bf(s);
       if (p.mask) p.mask[b * p.msb + h * p.msh + int64_t(t) * p.mst] = s > p.thr ? 1 : 0;
     }
@@ -535,9 +550,9 @@ constexpr int kDgaThreads = 128;
 struct DecodeGateParams {
   RowSrc in[3];  // selected gate inputs (concat order), token stride unused
   const uint16_t* norm[3];
-  int n_in, I, inner, act;
+  int n_in, I, inner, act;  // act: WGKV_GATE_SILU | WGKV_GATE_CONV bits
   const uint16_t *w1, *b1, *w2, *b2;
-  float eps, thr;
+  float eps, thr, floor;
 };
 
 // Optional decode prologue fused in front of the gate (modeling_llama.py:265-271, modeling_qwen3.py:
@@ -669,7 +684,7 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
         s = fmaf(xs[c * 8 + 2 * e + 1], __uint_as_float(ww[e] & 0xffff0000u), s);
       }
     }
-    const float hb = bf16_round(bf16_round(s) + bf2f(g.b1[h * g.inner + j]));
+    const float hb = gate_hidden(s, bf2f(g.b1[h * g.inner + j]), g.act);
     acc_out += bf16_round(act_fn(hb, g.act)) * bf2f(g.w2[h * g.inner + j]);
   }
   for (int o = 16; o; o >>= 1) acc_out += __shfl_xor_sync(0xffffffff, acc_out, o);
@@ -678,8 +693,7 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
   if (tid == 0) {
     float o = 0.f;
     for (int w = 0; w < kDgaThreads / 32; ++w) o += part[w];
-    o = bf16_round(bf16_round(o) + bf2f(g.b2[h]));
-    const float sc = bf16_round(1.f / (1.f + expf(-o)));
+    const float sc = gate_score(o, bf2f(g.b2[h]), g.act, g.floor);
     P.local_is_global[row] = sc > g.thr ? 1 : 0;  // ring slot `ins` of (layer, b, h)
   }
 }
@@ -700,16 +714,29 @@ bool ring_pos_ok(const wgkv_pool* P, int pos) {
 
 using namespace wgkv;
 
+// The conv path's clamp floor as torch applies it to a bf16 tensor: g_epsilon rounded to bf16
+// (round to nearest even); the fast path has no floor.
+static float gate_floor(int act, float score_floor) {
+  if (!(act & WGKV_GATE_CONV)) return -INFINITY;
+  uint32_t u;
+  memcpy(&u, &score_floor, 4);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
 extern "C" int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
                                 const uint16_t* post_k, int64_t k_sb, int64_t k_sh, int64_t k_st,
                                 const uint16_t* value, int64_t v_sb, int64_t v_sh, int64_t v_st, int batch,
                                 int kv_heads, int seq_len, int head_dim, int input_mask, const uint16_t* w1,
                                 const uint16_t* b1, const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w,
-                                float rms_eps, int inner, int act, float threshold, uint16_t* scores, int64_t s_sb,
+                                float rms_eps, int inner, int act, float score_floor, float threshold,
+                                uint16_t* scores, int64_t s_sb,
                                 int64_t s_sh, int64_t s_st, uint8_t* mask, int64_t m_sb, int64_t m_sh, int64_t m_st,
                                 void* stream) {
   if (batch <= 0 || kv_heads <= 0 || seq_len < 0 || (head_dim != 64 && head_dim != 128)) return WGKV_EINVAL;
-  if (inner <= 0 || inner % 8 != 0 || !w1 || !b1 || !w2 || !b2 || (act != 0 && act != 1)) return WGKV_EINVAL;
+  if (inner <= 0 || inner % 8 != 0 || !w1 || !b1 || !w2 || !b2 || (act & ~(WGKV_GATE_SILU | WGKV_GATE_CONV))) return WGKV_EINVAL;
   if (seq_len == 0) return WGKV_OK;
   GateParams p = {};
   const uint16_t* ins[3] = {pre_k, post_k, value};
@@ -741,6 +768,7 @@ extern "C" int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk
   p.b2 = b2;
   p.eps = rms_eps;
   p.thr = threshold;
+  p.floor = gate_floor(act, score_floor);
   p.scores = scores;
   p.ssb = s_sb;
   p.ssh = s_sh;
@@ -855,10 +883,11 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
                                        const uint16_t* k_new, int64_t k_sb, int64_t k_sh, const uint16_t* v_new,
                                        int64_t v_sb, int64_t v_sh, int input_mask, const uint16_t* w1,
                                        const uint16_t* b1, const uint16_t* w2, const uint16_t* b2,
-                                       const uint16_t* norm_w, float rms_eps, int inner, int act, float threshold,
-                                       int32_t* cache_seqlens, void* stream) {
+                                       const uint16_t* norm_w, float rms_eps, int inner, int act, float score_floor,
+                                       float threshold, int32_t* cache_seqlens, void* stream) {
   if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || !ring_pos_ok(pool, insert_pos) ||
-      !k_new || !v_new || !w1 || !b1 || !w2 || !b2 || inner <= 0 || (act != 0 && act != 1))
+      !k_new || !v_new || !w1 || !b1 || !w2 || !b2 || inner <= 0 ||
+      (act & ~(WGKV_GATE_SILU | WGKV_GATE_CONV)))
     return WGKV_EINVAL;
   if (((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
         reinterpret_cast<uintptr_t>(pre_k_new) | reinterpret_cast<uintptr_t>(w1)) & 3) ||
@@ -884,6 +913,7 @@ extern "C" int wgkv_decode_gate_append(const wgkv_pool* pool, int layer, int ins
   g.w1 = w1; g.b1 = b1; g.w2 = w2; g.b2 = b2;
   g.eps = rms_eps;
   g.thr = threshold;
+  g.floor = gate_floor(act, score_floor);
   PoolArgs pa{*pool};
   RowSrc K{k_new, k_sb, k_sh, 0}, V{v_new, v_sb, v_sh, 0};
   const int BH = pool->batch * pool->kv_heads;
@@ -899,7 +929,8 @@ extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert
                                     const uint16_t* rope_sin, const int64_t* position, int64_t n_positions,
                                     uint16_t* q_out, int input_mask, const uint16_t* w1, const uint16_t* b1,
                                     const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
-                                    int inner, int act, float threshold, int32_t* cache_seqlens, void* stream) {
+                                    int inner, int act, float score_floor, float threshold, int32_t* cache_seqlens,
+                                    void* stream) {
   if (!pool_ok(pool) || layer < 0 || layer >= pool->layers || !ring_pos_ok(pool, insert_pos) || !qkv || !rope_cos ||
       !rope_sin || !position || n_positions <= 0 || !q_out || q_heads <= 0 || q_heads % pool->kv_heads)
     return WGKV_EINVAL;
@@ -919,7 +950,8 @@ extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert
   R.n_pos = n_positions;
   R.q_out = q_out;
   if (w1) {
-    if (!b1 || !w2 || !b2 || inner <= 0 || (act != 0 && act != 1) || (reinterpret_cast<uintptr_t>(w1) & 15))
+    if (!b1 || !w2 || !b2 || inner <= 0 || (act & ~(WGKV_GATE_SILU | WGKV_GATE_CONV)) ||
+        (reinterpret_cast<uintptr_t>(w1) & 15))
       return WGKV_EINVAL;
     int n = 0;
     for (int s = 0; s < 3; ++s) {
@@ -936,6 +968,7 @@ extern "C" int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert
     g.w1 = w1; g.b1 = b1; g.w2 = w2; g.b2 = b2;
     g.eps = rms_eps;
     g.thr = threshold;
+    g.floor = gate_floor(act, score_floor);
   }
   PoolArgs pa{*pool};
   const int BH = pool->batch * pool->kv_heads;

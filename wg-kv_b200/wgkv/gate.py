@@ -4,9 +4,11 @@ The module keeps the reference's sub-module names and shapes
 (src/modeling_layers.py:134-160: ``pre_key_norm`` / ``post_key_norm`` /
 ``value_norm`` RMS norms, grouped 1x1 ``conv1`` and ``conv2``), so the
 published gate checkpoints (``model.layers.{i}.self_attn.g_predictors.*``)
-load with ``load_state_dict``.  ``forward`` runs the fast path
-(``:185-196``) as one sm_100a kernel (``wgkv_gate_scores``) and returns bf16
-scores of shape (B, Hk, L); :meth:`admit` writes the admission mask
+load with ``load_state_dict``.  ``forward`` runs as one sm_100a kernel
+(``wgkv_gate_scores``) with the numerics ``g_fast_path`` selects -- the einsum
+fast path (``:185-196``) or the grouped-conv path with its ``g_epsilon`` clamp
+(``:198-205``, the reference's default) -- and returns bf16 scores of shape
+(B, Hk, L); :meth:`admit` writes the admission mask
 ``scores > threshold`` straight into any uint8 tensor view (e.g. the
 cache's ``local_is_global`` slots) without materialising the scores.
 """
@@ -57,6 +59,7 @@ class GatingPredictor(nn.Module):
         self.input_dim = head_dim * len(self.g_inputs)
         self.inner_dim = int(head_dim * g_expand)
         self.g_rms = g_rms
+        # WGKV_GATE_SILU (0x1) / WGKV_GATE_CONV (0x2) bits of the entry points' `act` argument
         self.act = 1 if g_act_fn == "silu" else 0
         self.pre_key_norm = GatingRMSNorm(head_dim) if g_rms and "pre_k" in self.g_inputs else nn.Identity()
         self.post_key_norm = GatingRMSNorm(head_dim) if g_rms and "post_k" in self.g_inputs else nn.Identity()
@@ -88,6 +91,9 @@ class GatingPredictor(nn.Module):
                 return float(mod.variance_epsilon)
         return 1e-6
 
+    def _act_flags(self):
+        return self.act | (0 if self.g_fast_path else 2)
+
     def _launch(self, pre_key, post_key, value, threshold, scores, mask):
         ref = next(t for t in (pre_key, post_key, value) if t is not None)
         require_cuda(ref, "gate input")
@@ -108,12 +114,12 @@ class GatingPredictor(nn.Module):
         mp = (mask.data_ptr(), mask.stride(0), mask.stride(1), mask.stride(2)) if mask is not None else (0, 0, 0, 0)
         st = lib.wgkv_gate_scores(*pk, *kk, *vv, B, Hk, L, D, self.input_mask, w1.data_ptr(), b1.data_ptr(),
                                   w2.data_ptr(), b2.data_ptr(), nw.data_ptr() if nw is not None else None,
-                                  self._eps(), self.inner_dim, self.act, float(threshold), *sp, *mp,
+                                  self._eps(), self.inner_dim, self._act_flags(), float(self.g_epsilon), float(threshold), *sp, *mp,
                                   stream_ptr(ref.device))
         check(st, "wgkv_gate_scores")
 
     def forward(self, pre_key, post_key, value):
-        """g_scores (B, Hk, L) bf16 (GatingPredictor.forward fast path, :170-196)."""
+        """g_scores (B, Hk, L) bf16 (GatingPredictor.forward, :170-205)."""
         ref = post_key if post_key is not None else (pre_key if pre_key is not None else value)
         B, Hk, L, _ = ref.shape
         scores = torch.empty(B, Hk, L, dtype=torch.bfloat16, device=ref.device)
@@ -143,7 +149,8 @@ class GatingPredictor(nn.Module):
         st = lib.wgkv_decode_gate_append(pool_ref(cache), layer, insert_pos, cur_local_len, *pk, *kk, *vv,
                                          self.input_mask, w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
                                          nw.data_ptr() if nw is not None else None, self._eps(), self.inner_dim,
-                                         self.act, float(threshold), cache.cache_seqlens.data_ptr(),
+                                         self._act_flags(), float(self.g_epsilon), float(threshold),
+                                         cache.cache_seqlens.data_ptr(),
                                          stream_ptr(post_key.device))
         check(st, "wgkv_decode_gate_append")
 
@@ -160,9 +167,10 @@ class GatingPredictor(nn.Module):
                                                   self.conv2.bias))
             nw = self._norm_weights(qkv.device)
             gp = (self.input_mask, w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
-                  nw.data_ptr() if nw is not None else None, self._eps(), self.inner_dim, self.act)
+                  nw.data_ptr() if nw is not None else None, self._eps(), self.inner_dim, self._act_flags(),
+                  float(self.g_epsilon))
         else:
-            gp = (0, None, None, None, None, None, 0.0, 0, 0)
+            gp = (0, None, None, None, None, None, 0.0, 0, 0, 0.0)
         st = lib.wgkv_decode_prologue(pool_ref(cache), layer, insert_pos, cur_local_len, qkv.data_ptr(),
                                       qkv.stride(0), q_heads, q_norm.data_ptr() if q_norm is not None else None,
                                       k_norm.data_ptr() if k_norm is not None else None, float(qk_eps),
