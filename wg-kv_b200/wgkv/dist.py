@@ -3,8 +3,10 @@
 Nothing on the hot path exchanges data between GPUs: sequences (and KV heads)
 are independent in the gate, the compaction, the page tables, the indices and
 both attentions.  A job is therefore split into contiguous shards of
-sequences (or of KV heads), each rank owns its own paged pool, and the only
-collective is the timing reduction (max over ranks) used by the benchmark.
+sequences (or of KV heads), and each rank owns its own paged pool.  With
+sequence sharding the only collective is the timing reduction (max over
+ranks); with KV-head sharding the attention output projection around the
+path sums its partial products over ranks (``wgkv.tp``).
 """
 from __future__ import annotations
 
