@@ -45,6 +45,7 @@ QWEN3_CFG = dict(model="Qwen3-4B-shaped", layers=36, batch=64, ctx=32768, ctx_mi
                  threshold=0.5)
 WORKLOAD_NAME = "C2 decode: Llama-3.1-8B shape, B=16/GPU, 128K ctx, W=4096, T=16, Beta(2,8) admit"
 QWEN3_METRIC = "decode tok/s @8-32K mixed ragged cache (Qwen3-4B shape, B=64, 36 layers)"
+QWEN3_NAME = "C4 decode: Qwen3-4B shape, B=64/GPU, ctx U[8K,32K] per sequence, W=2048, T=16, Beta(1,10) admit"
 
 
 def _admit_params():
@@ -210,63 +211,44 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------
-# CPU arms (the oracle restatement of the reference algorithm)
+# CPU arms: the reference's PyTorch decode step on the host cores (oracle/torch_cpu_step.py)
 # ----------------------------------------------------------------------------
 
-def cpu_sample_step(seed=5):
-    """One bounded CPU sample: one sequence x one layer of the step (gate on
-    the new key, ring append, promotion, paged attention over the 8 heads at
-    the workload's length distribution).  Returns (callable, description)."""
-    from oracle import wgkv_oracle as O
-    Hk, Hq, D, W, T, ctx = (CFG[k] for k in ("kv_heads", "q_heads", "head_dim", "window", "page", "ctx"))
-    rate, glen = draw_lengths(2, 1, 1, Hk, ctx, W)
-    st = O.PoolState(layers=1, batch=1, kv_heads=Hk, head_dim=D, window=W, page=T,
-                     max_total_tokens=int((Hk * W + glen.sum() + Hk * 64) + 64) * 1,
-                     max_tokens_per_head=int(W + glen.max() + 256), defer=False)
-    rng = np.random.default_rng(seed)
-    st.k[:] = rng.standard_normal(st.k.shape, dtype=np.float32)
-    st.v[:] = rng.standard_normal(st.v.shape, dtype=np.float32)
-    nxt = st.next_free_block
-    for h in range(Hk):
-        n = int(glen[0, 0, h])
-        np_ = (n + T - 1) // T
-        st.block_table[0, 0, h, W // T:W // T + np_] = np.arange(nxt, nxt + np_)
-        nxt += np_
-        st.global_lengths[0, 0, h] = n
-    st.next_free_block = nxt
-    st.local_length = W
-    st.local_is_global[:] = rng.random(st.local_is_global.shape) < 0.2
-    inner = 64
-    p = O.GateParams(w1=O.bf16(rng.uniform(-0.09, 0.09, (Hk, inner, D)).astype(np.float32)),
-                     b1=O.bf16(rng.uniform(-0.09, 0.09, (Hk, inner)).astype(np.float32)),
-                     w2=O.bf16(rng.uniform(-0.12, 0.12, (Hk, inner)).astype(np.float32)), b2=np.zeros(Hk, np.float32))
-    q = O.randn_bf16(rng, (1, 1, Hq, D))
-    kn, vn, pk = (O.randn_bf16(rng, (1, Hk, 1, D)) for _ in range(3))
+def cpu_threads():
+    """Use every host core: torchrun sets OMP_NUM_THREADS=1 for its ranks."""
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_sample_step(layers_in_sample=2, seed=5):
+    """A bounded CPU sample of the workload's decode step: all ``batch`` sequences x
+    ``layers_in_sample`` layers at the GPU run's length distribution (rank 0's draw), with the
+    reference's operations in bf16 torch on the host.  Returns (callable, description, layers)."""
+    import torch
+    from oracle.torch_cpu_step import TorchCpuDecode
+    Ly, B, Hk, Hq, D, W, T, ctx = (CFG[k] for k in ("layers", "batch", "kv_heads", "q_heads", "head_dim", "window",
+                                                    "page", "ctx"))
+    S = min(layers_in_sample, Ly)
+    _, glen = draw_lengths(2, Ly, B, Hk, ctx, W)
+    st = TorchCpuDecode(S, B, Hk, Hq, D, W, T, glen[:S], steps=4096, seed=seed, threshold=CFG["threshold"])
+    g = torch.Generator().manual_seed(seed + 1)
+    q = torch.randn(S, B, Hq, D, generator=g).to(torch.bfloat16)
+    kn, vn, pk = (torch.randn(S, B, Hk, D, generator=g).to(torch.bfloat16) for _ in range(3))
 
     def run():
-        s = O.gate_scores(p, pre_key=pk)
-        st.promote()
-        cur = st.append_layer(0, kn[:, :, 0], vn[:, :, 0], O.admission_mask(s, CFG["threshold"])[:, :, 0])
-        sl, bt = st.decode_tables(0, cur)
-        kc, vc = st.paged_views()
-        O.paged_decode(q, kc, vc, sl, bt, D ** -0.5)
-        st.local_length = W  # keep the ring full for the next sample
-    desc = (f"1 sequence x 1 layer of the decode step (8 KV heads, {int((W + glen).sum())} cached tokens, "
-            f"gate+promote+append+attention), numpy oracle; tok/s = 1 / (t_sample x {CFG["layers"]} layers)")
-    return run, desc
-
-
-def blas_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
-    except Exception:
-        return os.cpu_count() or 1
+        st.step(q, kn, vn, pk)
+    tokens = int((W + glen[:S]).sum())
+    desc = (f"{B} sequences x {S} of {Ly} layers of the decode step ({tokens} cached tokens: gate, promotion, "
+            f"ring append, paged attention), the reference's torch operations in bf16 on the host "
+            f"(oracle/torch_cpu_step.py); tok/s = {B} / (t_sample x {Ly}/{S})")
+    return run, desc, S
 
 
 def time_cpu(budget_s=15.0, min_reps=2, max_reps=50):
-    run, desc = cpu_sample_step()
+    cores = cpu_threads()
+    run, desc, S = cpu_sample_step()
     run()  # warm
     t0 = time.perf_counter()
     reps = 0
@@ -274,25 +256,28 @@ def time_cpu(budget_s=15.0, min_reps=2, max_reps=50):
         run()
         reps += 1
     t = (time.perf_counter() - t0) / reps
-    return 1.0 / (t * CFG["layers"]), desc + f"; {reps} samples of {t * 1e3:.1f} ms"
+    return CFG["batch"] / (t * CFG["layers"] / S), desc + f"; {reps} samples of {t * 1e3:.1f} ms", cores
 
 
 def reference_arm(args, rank, world):
+    """The reference's kind of computation on the host cores: each step is one bounded sample (all
+    sequences x 1 layer of the decode step), run by rank 0 alone."""
     if rank != 0:
         return
-    run, desc = cpu_sample_step()
+    cores = cpu_threads()
+    run, desc, S = cpu_sample_step(layers_in_sample=1)
     for _ in range(args.warmup):
         run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         run()
     t = (time.perf_counter() - t0) / args.steps
-    val = 1.0 / (t * CFG["layers"])
-    cores = blas_threads()
+    val = CFG["batch"] / (t * CFG["layers"] / S)
     line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD_NAME + " (one step sample: 1 sequence x 1 layer)", **CFG},
+            "warmup": args.warmup, "ms_per_step": t * 1e3 * CFG["layers"] / S, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD_NAME + " (each step: one bounded sample, all sequences x 1 layer)",
+                       **CFG},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -302,7 +287,10 @@ def reference_arm(args, rank, world):
 # GPU arm
 # ----------------------------------------------------------------------------
 
-def gpu_arm(args, rank, world, local_rank):
+def gpu_arm(args, rank, world, local_rank, emit=True, steps=None, extras=True):
+    """The decode workload of CFG (C2 by default, C4 with --workload qwen3_decode).  The default run
+    (``extras``) adds the other BASELINE workloads as sub-records of its line: the 400K prefill (C3)
+    and the Qwen3-4B decode (C4) on one GPU, and the KV-head-sharded decode (C5) at every N."""
     import torch
     import torch.distributed as dist
     import wgkv
@@ -310,7 +298,8 @@ def gpu_arm(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     Ly, B, Hk, Hq, D = CFG["layers"], CFG["batch"], CFG["kv_heads"], CFG["q_heads"], CFG["head_dim"]
-    steps_total = args.warmup + 2 * args.steps + 8
+    K = steps if steps is not None else args.steps
+    steps_total = args.warmup + 2 * K + 8
     cache, rate, glen0 = build_state(dev, steps_total, seed=2 + 1000 * rank)
     layers = build_layers(dev, rate, seed=3 + 1000 * rank)
     NI = 4
@@ -350,14 +339,14 @@ def gpu_arm(args, rank, world, local_rank):
     glen_start = cache.global_lengths.cpu().numpy().astype(np.int64)
 
     # ---- device-resident timed region ----
-    clk = ClockSampler(local_rank) if rank == 0 else None
+    clk = ClockSampler(local_rank) if (rank == 0 and emit) else None
     barrier()
     torch.cuda.synchronize()
     l0 = wgkv.lib.launches
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("wgkv_timed")
     e0.record()
-    for s in range(args.steps):
+    for s in range(K):
         step(s)
     e1.record()
     torch.cuda.nvtx.range_pop()
@@ -369,8 +358,8 @@ def gpu_arm(args, rank, world, local_rank):
     wgkv.check_errors()
     glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
     ms = max_over_ranks(ms, dev)
-    ms_step = ms / args.steps
-    value = world * B * args.steps / (ms / 1e3)
+    ms_step = ms / K
+    value = world * B * K / (ms / 1e3)
     bytes_step, _ = algorithmic_bytes(cache, (glen_start + glen_end) / 2.0)
 
     # ---- end-to-end through the public API with host buffers ----
@@ -384,7 +373,7 @@ def gpu_arm(args, rank, world, local_rank):
     dev_q = [torch.empty_like(qbuf[0]) for _ in range(2)]
     dev_out = [torch.empty_like(outbuf) for _ in range(2)]
     host_out = [torch.empty(outbuf.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
-    e_steps = max(1, min(args.steps, 64))
+    e_steps = max(1, min(K, 64))
     main = torch.cuda.current_stream(dev)
     cs = torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
@@ -465,21 +454,41 @@ def gpu_arm(args, rank, world, local_rank):
     cache_gb = cache.block_pool_k.numel() * 4 / 1e9
     h2d_step = int((inputs[0].numel() + qbuf[0].numel()) * 2)  # the bytes the e2e loop uploads per step
     d2h_step = int(outbuf.numel() * 2)
-    prefill = None
-    if world == 1 and args.workload == "decode" and not args.no_prefill and not args.small:
-        # the 400K sparse prefill (C3) on the same GPU, decode cache released first
+    prefill = c4 = c5 = None
+    extras = extras and args.workload == "decode" and not args.small
+    if extras:
         del cache, layers, inputs, qbuf, outbuf, outs, host_in, host_q, dev_in, dev_q, host_out
         torch.cuda.empty_cache()
+    if extras and world == 1 and not args.no_prefill:
+        # the 400K sparse prefill (C3) on the same GPU, decode cache released first
         pl = prefill_arm(args, rank, world, local_rank, emit=False)
         prefill = {k: pl[k] for k in ("metric", "value", "unit", "admitted_frac", "tflops_step", "roofline",
-                                      "sparse_attn_func_gather_ms", "gpu_launches", "clocks")}
+                                      "sparse_attn_func_gather_ms", "kernels", "gpu_launches", "clocks")}
         prefill["workload"] = pl["config"]["workload"]
+        torch.cuda.empty_cache()
+    if extras and world == 1:
+        # C4: Qwen3-4B-shaped decode, batch 64, mixed 8-32K contexts
+        c4 = run_workload(QWEN3_CFG, lambda: gpu_arm(args, rank, world, local_rank, emit=False,
+                                                     steps=min(K, 64), extras=False))
+        c4 = {k: c4[k] for k in ("value", "unit", "ms_per_step", "hbm_gbs_step", "e2e", "roofline", "gpu_launches")}
+        c4.update(metric=QWEN3_METRIC, workload=QWEN3_NAME, steps=min(K, 64))
+        torch.cuda.empty_cache()
+    if extras:
+        # C5: KV heads sharded over the N GPUs of this run, o_proj all-reduce per layer
+        c5 = c5_arm(args, rank, world, local_rank, emit=False, steps=min(K, 16))
+        c5 = {k: c5[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling",
+                                 "per_gpu_tok_s", "per_layer_us", "per_layer_us_note", "e2e",
+                                 "attn_hbm_gbs_per_gpu", "attn_hbm_frac_per_gpu", "roofline", "gpu_launches")}
+        c5["config"] = {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
+                        "parallelism": f"tp{world} (KV heads)", "note": "resident layer pools cycled when the "
+                        "cache does not fit (N < 4)"}
+    line = None
     if rank == 0:
-        cpu_val, cpu_desc = (None, None)
-        if world == 1:
-            cpu_val, cpu_desc = time_cpu()
+        cpu_val, cpu_desc, cpu_cores = (None, None, None)
+        if world == 1 and emit:
+            cpu_val, cpu_desc, cpu_cores = time_cpu()
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD_NAME,
@@ -496,10 +505,28 @@ def gpu_arm(args, rank, world, local_rank):
         }
         if prefill is not None:
             line["prefill_400k"] = prefill
+        if c4 is not None:
+            line["c4_qwen3_decode"] = c4
+        if c5 is not None:
+            line["c5_decode"] = c5
         if cpu_val is not None:
-            line["cpu_baseline"] = {"value": cpu_val, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+            line["cpu_baseline"] = {"value": cpu_val, "unit": "tok/s", "cores": cpu_cores, "kind": "port",
                                     "sample": cpu_desc}
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
+    return line
+
+
+def run_workload(cfg, fn):
+    """Run ``fn`` with the decode globals (CFG) switched to ``cfg``, then restore them."""
+    saved = dict(CFG)
+    CFG.clear()
+    CFG.update(cfg)
+    try:
+        return fn()
+    finally:
+        CFG.clear()
+        CFG.update(saved)
 
 
 # ----------------------------------------------------------------------------
@@ -586,15 +613,17 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
     out = torch.empty_like(q)
     kk, vv = kvp[:, :, :Hk], kvp[:, :, Hk:2 * Hk]
 
-    def timed(fn):
+    def timed(fn, reps=3):
+        """Mean CUDA-event time of ``reps`` back-to-back calls after one warm-up call (ms)."""
         fn()
         torch.cuda.synchronize()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
-        fn()
+        for _ in range(reps):
+            fn()
         a1.record()
         torch.cuda.synchronize()
-        return a0.elapsed_time(a1)
+        return a0.elapsed_time(a1) / reps
 
     # the product path: admitted columns from layer 0's compacted pool (same mask as idx0)
     attn_ms = timed(lambda: wgkv.sparse_attn_func_pooled(q, kk, vv, *idx0, cache.block_pool_k, cache.block_pool_v,
@@ -604,6 +633,7 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
     gather_ms = timed(lambda: wgkv.sparse_attn_func(q, kk, vv, *idx0, softmax_scale=D ** -0.5, out=out))
     f0 = useful_flops(idx0[2].cpu().numpy(), L, W, D, G)
     tf = f0 / (attn_ms / 1e3) / 1e12
+    kernels = admission_kernel_rates(cache, layers[0], q, pk, k, v, L, W, T, D, Hk, timed)
     try:
         pk_tf = float(json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["bf16_tflops"]), "measured"
     except Exception:
@@ -616,6 +646,7 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
             "admitted_frac": admitted / (Ly * Hk * max(L - W, 1)),
             "useful_tflops_total": flops / 1e12, "tflops_step": flops / (ms / 1e3) / 1e12,
             "sparse_attn_func_gather_ms": gather_ms,
+            "kernels": kernels,
             "roofline": {"bound": "tensor", "kernel": "sparse_prefill_tc_kernel (pooled)", "achieved": tf, "peak": pk_tf[0],
                          "peak_kind": pk_tf[1], "unit": "TFLOP/s", "frac": tf / pk_tf[0], "traffic": None,
                          "ms_per_launch": attn_ms, "flops_per_launch": f0},
@@ -623,6 +654,61 @@ def prefill_arm(args, rank, world, local_rank, emit=True):
     if rank == 0 and emit:
         print(json.dumps(line), flush=True)
     return line
+
+
+def admission_kernel_rates(cache, a0, q, pk, k, v, L, W, T, D, Hk, timed):
+    """CUDA-event time and HBM rate of the admission kernels of one C3 layer (layer 0 of the run):
+    the gate (gate_kernel), the ring fill + compaction (chunk_count, prefill_alloc, prefill_scatter)
+    and the sparse-index builder, each against its algorithmic bytes:
+
+    * gate: pre_k read (2 B per element) + one mask byte per (head, token);
+    * compaction: mask read + K/V rows of the ring and of the admitted tokens read and written;
+    * indices: mask read + 4 B per admitted column index + the per-row-block counts and offsets.
+
+    The compaction is re-run on layer 0 of the finished cache with the allocator rewound to the
+    ring pages, so it rewrites the same pages with the same rows."""
+    import torch
+    import wgkv
+    from wgkv._lib import lib
+    from wgkv.pool import pool_ref
+    from wgkv.runtime import stream_ptr, workspace
+    peak, kind = peaks()
+    dev = q.device
+    thr = a0.config.g_threshold
+    gm = torch.empty(1, Hk, L, dtype=torch.uint8, device=dev)
+    g_ms = timed(lambda: a0.g_predictors.admit(pk, k, v, thr, gm))
+    n_adm = cache.global_lengths[0].to(torch.int64).sum().item()
+    g_bytes = Hk * L * (D * 2 + 1)
+    total_local = int(cache.block_table[..., :W // T].numel())
+    saved = cache.next_free_block.clone()
+    nbytes = int(lib.wgkv_prefill_admit_workspace_size(1, Hk, L - W))
+    ws = workspace(dev, "prefill_admit", nbytes)
+
+    def s4(t):
+        return t.data_ptr(), t.stride(0), t.stride(1), t.stride(2)
+
+    def compact():
+        cache.next_free_block.fill_(total_local)
+        lib.wgkv_prefill_admit(pool_ref(cache), 0, L, *s4(k), *s4(v), None, 0, 0, 0, *s4(gm), ws.data_ptr(),
+                               ws.numel(), stream_ptr(dev))
+
+    c_ms = timed(compact)
+    cache.next_free_block.copy_(saved)
+    c_bytes = Hk * L + (Hk * min(L, W) + n_adm) * D * 2 * 2 * 2
+    ci = torch.zeros(1, Hk, 1, L, dtype=torch.int32, device=dev)
+    mc = torch.zeros(1, dtype=torch.int32, device=dev)
+    i_ms = timed(lambda: wgkv.sparse_indices_into(gm, W, L, 64, column_index=ci, max_count=mc))
+    R = (L + 63) // 64
+    i_bytes = Hk * L + 4 * n_adm + 4 * Hk * R + 4 * R * (min(W // 64, R) + 2)
+    wgkv.check_errors()
+    out = {}
+    for name, ms, by, kern in (("gate", g_ms, g_bytes, "gate_kernel"),
+                               ("compaction", c_ms, c_bytes, "chunk_count + prefill_alloc + prefill_scatter"),
+                               ("sparse_indices", i_ms, i_bytes, "idx_count + idx_scan + idx_scatter (+ block offsets)")):
+        gbs = by / (ms / 1e3) / 1e9
+        out[name] = {"kernels": kern, "ms": ms, "algorithmic_bytes": by, "achieved_gbs": gbs, "peak_gbs": peak,
+                     "peak_kind": kind, "frac": gbs / peak}
+    return out
 
 
 # ----------------------------------------------------------------------------
@@ -633,17 +719,24 @@ C5_CFG = dict(model="Llama-3.1-8B-shaped", layers=32, batch=64, ctx=262144, q_he
               window=4096, page=16, admit="Beta(2,8)", gate="pre_k->64->1 GELU sigmoid", threshold=0.5, hidden=4096)
 
 
-def c5_arm(args, rank, world, local_rank):
+def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
+    """BASELINE config 5 through ``wgkv.tp.KVHeadParallelAttention``: this rank's KV heads and their
+    query heads, its own pool, the row-parallel o_proj slice of every layer and one all-reduce per
+    layer.  Returns the JSON record (printed by rank 0 when ``emit``)."""
     import torch
     import torch.distributed as dist
     import wgkv
     from wgkv.dist import kv_head_shard, max_over_ranks
+    from wgkv.tp import KVHeadParallelAttention, shard_o_proj
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    K = steps if steps is not None else args.steps
     Ly, B, D, W, T = C5_CFG["layers"], C5_CFG["batch"], C5_CFG["head_dim"], C5_CFG["window"], C5_CFG["page"]
-    (h0, h1), (q0, q1) = kv_head_shard(C5_CFG["kv_heads"], C5_CFG["q_heads"], rank, world)
+    Hq_all, Hk_all, hidden = C5_CFG["q_heads"], C5_CFG["kv_heads"], C5_CFG["hidden"]
+    (h0, h1), (q0, q1) = kv_head_shard(Hk_all, Hq_all, rank, world)
     Hk, Hq = h1 - h0, q1 - q0
     # resident layer pools: all 32 when they fit in ~150 GB, else as many as fit, cycled over the 32 layers
+    saved = dict(CFG)
     CFG.clear()
     CFG.update(C5_CFG)
     CFG["kv_heads"], CFG["q_heads"] = Hk, Hq
@@ -651,55 +744,75 @@ def c5_arm(args, rank, world, local_rank):
     per_layer = float(((W + glen) * D * 2 * 2).sum()) * 1.02
     resident = int(max(1, min(Ly, 150e9 // per_layer)))
     CFG["layers"] = resident
-    steps_total = args.warmup + args.steps + 8 + 16  # + the end-to-end steps
+    steps_total = args.warmup + K + 8 + 16 + 4  # + the end-to-end and instrumented steps
     cache, rate, glen0 = build_state(dev, steps_total * ((Ly + resident - 1) // resident), seed=2 + 1000 * rank)
     layers = build_layers(dev, rate, seed=3 + 1000 * rank)
+    CFG.clear()
+    CFG.update(saved)
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
     NI = 4
     inputs = torch.randn(NI, Ly, B, 1, Hq + 3 * Hk, D, generator=g, device=dev).to(torch.bfloat16)
     qbuf = inputs[..., :Hq, :].contiguous()
-    hidden = C5_CFG["hidden"]
-    wo = (torch.randn(hidden, Hq * D, generator=g, device=dev) * (Hq * D * world) ** -0.5).to(torch.bfloat16)
+    # every layer its own W_o (hidden, 32 * 128); this rank keeps the columns of its query heads
+    gw = torch.Generator(device=dev)
+    gw.manual_seed(99)  # same full weights on every rank
+    tp_layers = []
+    for l in range(Ly):
+        w_full = (torch.randn(hidden, Hq_all * D, generator=gw, device=dev) * (Hq_all * D) ** -0.5).to(torch.bfloat16)
+        tp_layers.append(KVHeadParallelAttention(layers[l % resident], shard_o_proj(w_full, q0, q1, D)))
+        del w_full
     y = torch.empty(B, hidden, dtype=torch.bfloat16, device=dev)
 
     def step(s, xin=None, qin=None):
         for l in range(Ly):
-            a = layers[l % resident]
             x = inputs[s % NI, l] if xin is None else xin[l]
             q = (qbuf[s % NI, l] if qin is None else qin[l]).transpose(1, 2)
             k = x[:, :, Hq:Hq + Hk].transpose(1, 2)
             v = x[:, :, Hq + Hk:Hq + 2 * Hk].transpose(1, 2)
             pk = x[:, :, Hq + 2 * Hk:].transpose(1, 2)
-            o, _, _ = a.self_attn_forward_patch(a, 3, None, cache, (B, 1), q, pk, k, v)
-            # row-parallel o_proj on this GPU's heads, summed over GPUs (the only exchange)
-            torch.matmul(o.view(B, Hq * D), wo.t(), out=y)
-            if world > 1:
-                dist.all_reduce(y)
+            tp_layers[l](cache, (B, 1), q, pk, k, v, out=y)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
 
     for s in range(args.warmup):
         step(s)
     torch.cuda.synchronize()
     wgkv.check_errors()
     glen_start = cache.global_lengths.cpu().numpy().astype(np.int64)
-    if world > 1:
-        dist.barrier()
+    barrier()
     torch.cuda.synchronize()
-    clk = ClockSampler(local_rank) if rank == 0 else None
+    clk = ClockSampler(local_rank) if (rank == 0 and emit) else None
     l0 = wgkv.lib.launches
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for s in range(args.steps):
+    for s in range(K):
         step(s)
     e1.record()
     torch.cuda.synchronize()
     launches = wgkv.lib.launches - l0
-    if world > 1:
-        dist.barrier()
+    barrier()
     clocks = clk.stop() if clk else None
-    ms = max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
+    ms = max_over_ranks(e0.elapsed_time(e1), dev) / K
     wgkv.check_errors()
     glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
+
+    # per-layer phases (CUDA events around attention, o_proj and the all-reduce) on 2 extra steps
+    for t in tp_layers:
+        t.timers = {}
+    barrier()
+    for s in range(2):
+        step(s)
+    torch.cuda.synchronize()
+    phase = {}
+    for key in ("attn", "o_proj", "all_reduce"):
+        vals = [x for t in tp_layers for x in t.breakdown().get(key, [])]
+        phase[key] = 1e3 * float(np.median(vals)) if vals else 0.0
+    for t in tp_layers:
+        t.timers = None
+    phase = {k: max_over_ranks(v, dev) for k, v in phase.items()}
 
     # end to end: each step's q/k/v/pre-k rows come from pinned host memory and the step's output
     # (the last layer's all-reduced o_proj rows) goes back, double-buffered on a copy stream
@@ -711,12 +824,11 @@ def c5_arm(args, rank, world, local_rank):
     dev_q = [torch.empty_like(qbuf[0]) for _ in range(2)]
     dev_y = [torch.empty_like(y) for _ in range(2)]
     host_y = [torch.empty(y.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
-    e_steps = max(1, min(args.steps, 16))
+    e_steps = max(1, min(K, 16))
     main = torch.cuda.current_stream(dev)
     cs = torch.cuda.Stream(dev)
     in_ready, in_free, out_ready, out_free = ([torch.cuda.Event(), torch.cuda.Event()] for _ in range(4))
-    if world > 1:
-        dist.barrier()
+    barrier()
     torch.cuda.synchronize()
     e6, e7 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e6.record()
@@ -749,8 +861,7 @@ def c5_arm(args, rank, world, local_rank):
     main.wait_stream(cs)
     e7.record()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    barrier()
     e2e = B * e_steps / (max_over_ranks(e6.elapsed_time(e7), dev) / 1e3)
     wgkv.check_errors()
     # per-GPU attention bytes per step (32 layer visits over the resident pools)
@@ -774,26 +885,38 @@ def c5_arm(args, rank, world, local_rank):
     kbytes = float(seq0.sum().item()) * D * 2 * 2
     peak, peak_kind = peaks()
     ach = kbytes / (kms / 1e3) / 1e9
-    if rank == 0:
-        line = {"metric": "decode tok/s @256K ragged cache, KV heads sharded (Llama-8B shape, B=64, 32 layers)",
-                "value": B / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
-                           "resident_layer_pools": resident,
-                           "note": ("all 32 layer pools resident" if resident == Ly else
-                                    f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
-                           "parallelism": f"tp{world} (KV heads)", **C5_CFG},
-                "per_gpu_tok_s": B / (ms / 1e3) / world,
-                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int((inputs[0].numel() + qbuf[0].numel()) * 2),
-                        "d2h_bytes_per_step": int(y.numel() * 2)},
-                "gpu_launches": launches,
-                "attn_hbm_gbs_per_gpu": attn_bytes / (ms / 1e3) / 1e9,
-                "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": ach, "peak": peak,
-                             "peak_kind": peak_kind, "unit": "GB/s", "frac": ach / peak, "ms_per_launch": kms,
-                             "bytes_per_launch": kbytes},
-                "clocks": clocks}
+    del cache, layers, tp_layers, inputs, qbuf, host_in, host_q
+    torch.cuda.empty_cache()
+    line = {"metric": "decode tok/s @256K ragged cache, KV heads sharded (Llama-8B shape, B=64, 32 layers)",
+            "value": B / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
+                       "resident_layer_pools": resident,
+                       "note": ("all 32 layer pools resident" if resident == Ly else
+                                f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
+                       "parallelism": f"tp{world} (KV heads)", **C5_CFG},
+            "per_gpu_tok_s": B / (ms / 1e3) / world,
+            "per_layer_us": {k: v for k, v in phase.items()},
+            "per_layer_us_note": ("median over 2 instrumented steps x 32 layers, max over ranks; all_reduce "
+                                  "includes waiting for the slowest rank"),
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(host_in_bytes(NI, Ly, B, Hq, Hk, D)),
+                    "d2h_bytes_per_step": int(B * hidden * 2)},
+            "gpu_launches": launches,
+            "attn_hbm_gbs_per_gpu": attn_bytes / (ms / 1e3) / 1e9,
+            "attn_hbm_frac_per_gpu": attn_bytes / (ms / 1e3) / 1e9 / peak,
+            "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel<128>", "achieved": ach, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": ach / peak, "ms_per_launch": kms,
+                         "bytes_per_launch": kbytes},
+            "clocks": clocks}
+    if rank == 0 and emit:
         print(json.dumps(line), flush=True)
+    return line
+
+
+def host_in_bytes(NI, Ly, B, Hq, Hk, D):
+    """Bytes the C5 end-to-end loop uploads per step: q/k/v/pre-k rows of every layer + the q copy."""
+    return Ly * B * (Hq + 3 * Hk) * D * 2 + Ly * B * Hq * D * 2
 
 
 def quest_arm(args, rank, world, local_rank):
@@ -1050,8 +1173,7 @@ def main():
         CFG.clear()
         CFG.update(QWEN3_CFG)
         METRIC = QWEN3_METRIC
-        WORKLOAD_NAME = ("C4 decode: Qwen3-4B shape, B=64/GPU, ctx U[8K,32K] per sequence, W=2048, T=16, "
-                         "Beta(1,10) admit")
+        WORKLOAD_NAME = QWEN3_NAME
     if args.small and args.workload != "prefill":
         CFG["layers"] = 2
     rank = int(os.environ.get("RANK", 0))
