@@ -457,7 +457,9 @@ def gpu_arm(args, rank, world, local_rank, emit=True, steps=None, extras=True):
     prefill = c4 = c5 = None
     extras = extras and args.workload == "decode" and not args.small
     if extras:
+        # release the decode state (the pool views of the roofline timing included) before the next workload
         del cache, layers, inputs, qbuf, outbuf, outs, host_in, host_q, dev_in, dev_q, host_out
+        del kc, vc, gl, seq_l, qd, qs, od
         torch.cuda.empty_cache()
     if extras and world == 1 and not args.no_prefill:
         # the 400K sparse prefill (C3) on the same GPU, decode cache released first

@@ -105,10 +105,18 @@ def test_c3_prefill_layer_400k():
     assert np.array_equal(cache.global_lengths.cpu().numpy(), st.global_lengths)
     assert np.array_equal(cache.local_is_global.cpu().numpy().astype(bool), st.local_is_global)
     assert int(cache.next_free_block.item()) == st.next_free_block
-    used = st.next_free_block * T
-    assert np.array_equal(_host(cache.block_pool_k[:used, :8]), st.k[:used])
-    assert np.array_equal(_host(cache.block_pool_v[:used, :8]), st.v[:used])
+    # rows the prefill writes: every ring row, and each head's admitted rows (a head's last page is
+    # written only up to its length; the rest of that page is unwritten in both)
     lp = W // T
+    written = np.zeros(st.next_free_block * T, bool)
+    written[:Hk * W] = True
+    for h in range(Hk):
+        first = int(st.block_table[0, 0, h, lp]) if st.global_lengths[0, 0, h] else 0
+        written[first * T:first * T + int(st.global_lengths[0, 0, h])] = True
+    rows_w = torch.from_numpy(np.flatnonzero(written)).to(dev)
+    nw = written.size
+    assert np.array_equal(_host(cache.block_pool_k[rows_w, :8]), st.k[:nw][written])
+    assert np.array_equal(_host(cache.block_pool_v[rows_w, :8]), st.v[:nw][written])
     for h in range(Hk):
         n = int(st.global_lengths[0, 0, h])
         pages = cache.block_table[0, 0, h, lp:lp + (n + T - 1) // T].long()

@@ -97,26 +97,34 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // ---- stage the input rows (concat + optional RMS norm) as bf16 ----------
+  // Each warp owns rows warp, warp + 8, ...: all of its rows' loads for one input are issued before
+  // any is used (kRowsPerWarp independent 8-byte loads per lane in flight), so the staging runs at
+  // memory throughput rather than one row latency after another.
+  constexpr int kRowsPerWarp = kGateRows / (kGateThreads / 32);
   const int per = p.D / 32;  // elements per lane per input (2 or 4)
-  for (int r = warp; r < kGateRows; r += kGateThreads / 32) {
-    const int gr = row0 + r;
-    uint16_t* dst = xs + r * RS;
-    if (gr >= nrows) {
-      for (int e = lane; e < I; e += 32) dst[e] = 0;
-      continue;
-    }
-    const int b = gr / p.L, t = gr - b * p.L;
-    for (int s = 0; s < p.n_in; ++s) {
-      const uint16_t* src = p.in[s] + b * p.sb[s] + h * p.sh[s] + int64_t(t) * p.st[s];
-      float x[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < p.n_in; ++s) {
+    uint32_t raw[kRowsPerWarp][2];
 #pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        if (j < per) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(src + lane * per + j);
-          x[j] = __uint_as_float(w << 16);
-          x[j + 1] = __uint_as_float(w & 0xffff0000u);
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int gr = row0 + warp + i * (kGateThreads / 32);
+      raw[i][0] = raw[i][1] = 0u;
+      if (gr < nrows) {
+        const int b = gr / p.L, t = gr - b * p.L;
+        const uint16_t* src = p.in[s] + b * p.sb[s] + h * p.sh[s] + int64_t(t) * p.st[s] + lane * per;
+        if (per == 4) {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(src));
+          raw[i][0] = w.x;
+          raw[i][1] = w.y;
+        } else {
+          raw[i][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int r = warp + i * (kGateThreads / 32);
+      float x[4] = {__uint_as_float(raw[i][0] << 16), __uint_as_float(raw[i][0] & 0xffff0000u),
+                    __uint_as_float(raw[i][1] << 16), __uint_as_float(raw[i][1] & 0xffff0000u)};
       if (p.norm[s]) {
         // GatingRMSNorm.forward (:123-128): fp32 variance, x * rsqrt(var + eps) -> bf16, * weight -> bf16
         float ss = 0.f;
@@ -132,9 +140,10 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
           }
         }
       }
-#pragma unroll
-      for (int j = 0; j < 4; j += 2)
-        if (j < per) *reinterpret_cast<uint32_t*>(dst + s * p.D + lane * per + j) = pack_bf16x2(x[j], x[j + 1]);
+      // rows past the end stay zero (their loads were skipped, and the norm of zeros is zero)
+      uint16_t* dst = xs + r * RS + s * p.D + lane * per;
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(x[0], x[1]);
+      if (per == 4) *reinterpret_cast<uint32_t*>(dst + 2) = pack_bf16x2(x[2], x[3]);
     }
   }
 
