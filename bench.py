@@ -479,9 +479,9 @@ def gpu_arm(args, rank, world, local_rank, emit=True, steps=None, extras=True):
         # C5: KV heads sharded over the N GPUs of this run, o_proj all-reduce per layer
         c5 = c5_arm(args, rank, world, local_rank, emit=False, steps=min(K, 16))
         c5 = {k: c5[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling",
-                                 "per_gpu_tok_s", "per_layer_us", "per_layer_us_note", "e2e",
+                                 "per_gpu_tok_s", "per_layer_us", "per_layer_us_note", "nccl_baseline", "e2e",
                                  "attn_hbm_gbs_per_gpu", "attn_hbm_frac_per_gpu", "roofline", "gpu_launches")}
-        c5["config"] = {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
+        c5["config"] = {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + sum over GPUs fused",
                         "parallelism": f"tp{world} (KV heads)", "note": "resident layer pools cycled when the "
                         "cache does not fit (N < 4)"}
     line = None
@@ -729,7 +729,7 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     import torch.distributed as dist
     import wgkv
     from wgkv.dist import kv_head_shard, max_over_ranks
-    from wgkv.tp import KVHeadParallelAttention, shard_o_proj
+    from wgkv.tp import KVHeadParallelAttention, PeerGroup, shard_o_proj
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     K = steps if steps is not None else args.steps
@@ -759,10 +759,12 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     # every layer its own W_o (hidden, 32 * 128); this rank keeps the columns of its query heads
     gw = torch.Generator(device=dev)
     gw.manual_seed(99)  # same full weights on every rank
+    # o_proj + sum over GPUs as one kernel over NVLink peer memory (the NCCL path is timed beside it)
+    peers = PeerGroup(max_rows=B, max_cols=hidden, device=dev)
     tp_layers = []
     for l in range(Ly):
         w_full = (torch.randn(hidden, Hq_all * D, generator=gw, device=dev) * (Hq_all * D) ** -0.5).to(torch.bfloat16)
-        tp_layers.append(KVHeadParallelAttention(layers[l % resident], shard_o_proj(w_full, q0, q1, D)))
+        tp_layers.append(KVHeadParallelAttention(layers[l % resident], shard_o_proj(w_full, q0, q1, D), peers=peers))
         del w_full
     y = torch.empty(B, hidden, dtype=torch.bfloat16, device=dev)
 
@@ -801,20 +803,42 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     wgkv.check_errors()
     glen_end = cache.global_lengths.cpu().numpy().astype(np.int64)
 
-    # per-layer phases (CUDA events around attention, o_proj and the all-reduce) on 2 extra steps
+    def phases():
+        """Per-layer phase times (CUDA events around attention and the projection / sum) on 2 extra steps."""
+        for t in tp_layers:
+            t.timers = {}
+        barrier()
+        for s in range(2):
+            step(s)
+        torch.cuda.synchronize()
+        out = {}
+        for key in ("attn", "o_proj_allreduce", "o_proj", "all_reduce"):
+            vals = [x for t in tp_layers for x in t.breakdown().get(key, [])]
+            if vals:
+                out[key] = max_over_ranks(1e3 * float(np.median(vals)), dev)
+        for t in tp_layers:
+            t.timers = None
+        return out
+
+    phase = phases()
+
+    # the same step with the unfused projection: torch GEMM + NCCL all-reduce (the baseline)
     for t in tp_layers:
-        t.timers = {}
+        t.peers = None
+    nccl_steps = max(1, min(K, 8))
     barrier()
-    for s in range(2):
-        step(s)
     torch.cuda.synchronize()
-    phase = {}
-    for key in ("attn", "o_proj", "all_reduce"):
-        vals = [x for t in tp_layers for x in t.breakdown().get(key, [])]
-        phase[key] = 1e3 * float(np.median(vals)) if vals else 0.0
+    e8, e9 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e8.record()
+    for s in range(nccl_steps):
+        step(s)
+    e9.record()
+    torch.cuda.synchronize()
+    nccl_ms = max_over_ranks(e8.elapsed_time(e9), dev) / nccl_steps
+    nccl_phase = phases()
     for t in tp_layers:
-        t.timers = None
-    phase = {k: max_over_ranks(v, dev) for k, v in phase.items()}
+        t.peers = peers
+    wgkv.check_errors()
 
     # end to end: each step's q/k/v/pre-k rows come from pinned host memory and the step's output
     # (the last layer's all-reduced o_proj rows) goes back, double-buffered on a copy stream
@@ -887,21 +911,27 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     kbytes = float(seq0.sum().item()) * D * 2 * 2
     peak, peak_kind = peaks()
     ach = kbytes / (kms / 1e3) / 1e9
-    del cache, layers, tp_layers, inputs, qbuf, host_in, host_q
+    barrier()
+    torch.cuda.synchronize()
+    peers.close()
+    del cache, layers, tp_layers, inputs, qbuf, host_in, host_q, peers
     torch.cuda.empty_cache()
     line = {"metric": "decode tok/s @256K ragged cache, KV heads sharded (Llama-8B shape, B=64, 32 layers)",
             "value": B / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + NCCL all-reduce",
+            "config": {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + sum over GPUs fused "
+                                   "(one kernel over NVLink peer memory)",
                        "resident_layer_pools": resident,
                        "note": ("all 32 layer pools resident" if resident == Ly else
                                 f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
                        "parallelism": f"tp{world} (KV heads)", **C5_CFG},
             "per_gpu_tok_s": B / (ms / 1e3) / world,
-            "per_layer_us": {k: v for k, v in phase.items()},
-            "per_layer_us_note": ("median over 2 instrumented steps x 32 layers, max over ranks; all_reduce "
-                                  "includes waiting for the slowest rank"),
+            "per_layer_us": phase,
+            "per_layer_us_note": ("median over 2 instrumented steps x 32 layers, max over ranks; the sum over "
+                                  "GPUs includes waiting for the slowest rank"),
+            "nccl_baseline": {"what": "same step with torch GEMM + NCCL all-reduce for o_proj", "steps": nccl_steps,
+                              "ms_per_step": nccl_ms, "value": B / (nccl_ms / 1e3), "per_layer_us": nccl_phase},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(host_in_bytes(NI, Ly, B, Hq, Hk, D)),
                     "d2h_bytes_per_step": int(B * hidden * 2)},
             "gpu_launches": launches,

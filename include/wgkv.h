@@ -30,6 +30,8 @@
  *   wgkv_snapkv_evict         snapkv_evict :595-671 (free list reused by promotion :694-709)
  *   wgkv_paged_decode         flash_attn_with_kvcache_wrapper_triton_handle + split/reduce kernels :818-1140
  *                             (and the batched flash_attn_with_kvcache_wrapper :766-811)
+ *   wgkv_oproj_allreduce      self.o_proj(attn_output) (src/modeling_llama.py:286) of a KV-head-sharded
+ *                             layer plus the sum over GPUs (the reference has no tensor parallelism)
  */
 #ifndef WGKV_H_
 #define WGKV_H_
@@ -239,6 +241,52 @@ WGKV_API int wgkv_decode_prologue(const wgkv_pool* pool, int layer, int insert_p
                                   const uint16_t* w2, const uint16_t* b2, const uint16_t* norm_w, float rms_eps,
                                   int inner, int act, float score_floor, float threshold, int32_t* cache_seqlens,
                                   void* stream);
+
+/* ---- KV-head tensor parallelism: o_proj fused with the sum over GPUs ------ */
+#define WGKV_TP_MAX_WORLD 8
+
+/*
+ * One GPU's view of a tensor-parallel group (one process per GPU).  partial[r] / flags[r] are rank
+ * r's buffers as mapped in this process (this rank's own pointers at index `rank`, the peers' through
+ * CUDA IPC: wgkv_ipc_handle / wgkv_ipc_open).  partial: wgkv_tp_partial_bytes(max_rows, max_cols),
+ * 16-byte aligned; flags: wgkv_tp_flag_bytes(max_cols), zeroed before first use; ctr: two uint32 of
+ * this GPU, zeroed before first use.  All ranks must use the same max_rows / max_cols.
+ */
+typedef struct wgkv_peer_group {
+  int32_t rank;
+  int32_t world;
+  int32_t max_rows;
+  int32_t max_cols;
+  void* partial[WGKV_TP_MAX_WORLD];
+  uint32_t* flags[WGKV_TP_MAX_WORLD];
+  uint32_t* ctr;
+} wgkv_peer_group;
+
+WGKV_API size_t wgkv_tp_partial_bytes(int max_rows, int max_cols);
+WGKV_API size_t wgkv_tp_flag_bytes(int max_cols);
+
+/*
+ * Export / import a device buffer for the peers of a group.  wgkv_ipc_handle writes the 64-byte
+ * CUDA IPC handle of the allocation holding `ptr` and ptr's byte offset in it; wgkv_ipc_open maps a
+ * peer's allocation into this process (base address; add the peer's offset), wgkv_ipc_close unmaps.
+ */
+WGKV_API int wgkv_ipc_handle(const void* ptr, void* handle_out, size_t* offset_out);
+WGKV_API int wgkv_ipc_open(const void* handle, void** base_out);
+WGKV_API int wgkv_ipc_close(void* base);
+
+/*
+ * y (rows, n_out) bf16 = sum over the group's GPUs of a_r (rows, k) . w_r^T, w_r (n_out, k) the
+ * columns of W_o that multiply this GPU's query heads (row-parallel o_proj).  One kernel: each CTA
+ * computes 32 output columns of this GPU's product (mma.sync, fp32 accumulate, rounded to bf16 as
+ * the unfused GEMM output is), publishes them to the peers and sums the peers' copies of the same
+ * columns in rank order (fp32), so every GPU gets identical bits.  Every rank must make the same
+ * sequence of calls (same rows, n_out) on its own stream; with world == 1 it is the plain GEMM.
+ * Waits on peers are bounded (~2 s): a peer that never arrives sets WGKV_ERR_TIMEOUT in err and the
+ * call completes with undefined y.  k % 64 == 0, n_out % 32 == 0, n_out / 32 <= the SM count,
+ * rows <= max_rows, 16-byte aligned rows.
+ */
+WGKV_API int wgkv_oproj_allreduce(const uint16_t* a, int64_t lda, int rows, int k, const uint16_t* w, int n_out,
+                                  uint16_t* y, int64_t ldy, const wgkv_peer_group* group, int* err, void* stream);
 
 /* ---- QUEST block selection (use_quest) ------------------------------------ */
 /*

@@ -67,3 +67,22 @@ def test_kv_head_shards_sum_to_unsharded(world):
         assert torch.equal(c.global_lengths, c_full.global_lengths[:, :, h0:h1])
         assert torch.equal(c.local_is_global, c_full.local_is_global[:, :, h0:h1])
     assert int(c_full.global_lengths.min()) > 0  # prefill admitted some tokens to every head
+
+
+@pytest.mark.parametrize("rows,k", [(64, 512), (5, 4096), (130, 1024)])
+def test_fused_oproj_group_of_one_is_the_gemm(rows, k):
+    """``wgkv_oproj_allreduce`` in a group of one GPU is the row-parallel GEMM itself: compared with an
+    fp32 torch matmul of the same bf16 operands (the kernel rounds its fp32 accumulator once)."""
+    from wgkv.tp import PeerGroup
+    g = torch.Generator(device="cuda").manual_seed(rows + k)
+    n_out = 4096
+    a = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n_out, k, generator=g, device="cuda") * k ** -0.5).bfloat16()
+    peers = PeerGroup(max_rows=256, max_cols=n_out)
+    y = torch.empty(rows, n_out, dtype=torch.bfloat16, device="cuda")
+    for _ in range(3):  # repeated calls advance the device epoch
+        peers.oproj_allreduce(a, w, y)
+    torch.cuda.synchronize()
+    import wgkv
+    wgkv.check_errors()
+    torch.testing.assert_close(y.float(), a.float() @ w.float().t(), atol=ATOL, rtol=RTOL)

@@ -47,9 +47,11 @@ struct Tc {
   static constexpr int kOffBar = kOffV + kStg * kKV;
   static constexpr int kOffX = kOffBar + 512;        // row-max / row-sum exchange [3][NM][2][128] floats
   static constexpr int kSmem = kOffX + 3 * NM * 2 * 128 * 4 + 1024;  // + alignment slack
-  // producer, MMA, then per M-tile two softmax warpgroups (one per 64-key half) or, with RW, one
-  // warpgroup whose threads each own a whole 128-key row
-  static constexpr int kThreads = 64 + (RW ? 128 : 256) * NM;
+  // producer, MMA, then per M-tile two softmax warpgroups (one per 64-key half) or, with RW, a
+  // first warpgroup (producer, MMA, two idle warps) and one warpgroup per M-tile whose threads each
+  // own a whole 128-key row
+  static constexpr int kThreads = RW ? 128 + 128 * NM : 64 + 256 * NM;
+  static constexpr int kSoftWarp0 = RW ? 4 : 2;      // first softmax warp
   static constexpr int kSoftWarps = RW ? 4 : 8;      // softmax warps per M-tile
   static constexpr int kTmemCols = NM == 2 ? 512 : 256;
 };
@@ -61,6 +63,60 @@ WGKV_DEV float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// Paired fp32 arithmetic (sm_100 f32x2 instructions): two lanes of a 64-bit register pair per
+// instruction, same rounding as the scalar forms.
+WGKV_DEV uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+WGKV_DEV void f2_split(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+WGKV_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+WGKV_DEV uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+WGKV_DEV float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA pipe for a pair of lanes, to take part of the softmax exponentials off the SFU
+// (which would otherwise bound the softmax): x = n + r with n = round(x) (the 1.5 * 2^23 shifter),
+// r in [-1/2, 1/2]; 2^r from a cubic fitted here to 2^r on [-1/2, 1/2] by least squares in relative
+// error at Chebyshev nodes (max relative error 7.7e-5, far below the bf16 rounding P gets); 2^n
+// added to the exponent field.  Inputs below -120 (masked keys are -inf) give 2^-120, zero for
+// every practical purpose next to a row sum >= 1.
+WGKV_DEV uint64_t exp2_fma2(uint64_t x) {
+  float a, b;
+  f2_split(x, a, b);
+  x = f2(fmaxf(a, -120.f), fmaxf(b, -120.f));
+  const uint64_t t = add2(x, f2(12582912.f, 12582912.f));
+  const uint64_t r = fma2(add2(t, f2(-12582912.f, -12582912.f)), f2(-1.f, -1.f), x);
+  uint64_t q = fma2(f2(0.05508868f, 0.05508868f), r, f2(0.24260405f, 0.24260405f));
+  q = fma2(q, r, f2(0.69327624f, 0.69327624f));
+  q = fma2(q, r, f2(0.99992894f, 0.99992894f));
+  float ta, tb, qa, qb;
+  f2_split(t, ta, tb);
+  f2_split(q, qa, qb);
+  // the shifter's low mantissa bits hold n; shifted by 23 they are n in the exponent field
+  return f2(__int_as_float(__float_as_int(ta) * (1 << 23) + __float_as_int(qa)),
+            __int_as_float(__float_as_int(tb) * (1 << 23) + __float_as_int(qb)));
+}
+
+#ifndef WGKV_EMU_PERIOD
+#define WGKV_EMU_PERIOD 4  // of every WGKV_EMU_PERIOD pairs of P, WGKV_EMU_COUNT use exp2_fma2
+#endif
+#ifndef WGKV_EMU_COUNT
+#define WGKV_EMU_COUNT 1
+#endif
 
 struct TcParams {
   int B, L, Hk, G, R, n_hg;
@@ -75,6 +131,14 @@ struct TcParams {
   int64_t t_stride;
   int t_first, t_page;
 };
+
+#ifdef WGKV_EXPERIMENT_TRACE  // timing experiment only: clock64 stamps of one CTA's pipeline events
+__device__ long long g_trace[16][256];
+#define WGKV_TRACE(row, j)                                                                     \
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) >= 0 && (j) < 256) g_trace[row][j] = clock64();
+#else
+#define WGKV_TRACE(row, j)
+#endif
 
 struct Bars {
   uint64_t qfull;
@@ -130,7 +194,11 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem;
   bool ok = true;
-
+  // RW with two M-tiles: 384 threads launched at 168 registers; the first warpgroup (producer, MMA)
+  // gives registers up to the two softmax warpgroups (128 x 56 + 256 x 224 = 384 x 168)
+  constexpr bool kRegSplit = RW && NM == 2;
+  if (warp < C::kSoftWarp0) {
+  if constexpr (kRegSplit) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
   if (warp == 0) {
     // ================================ producer ================================
     if (lane == 0) {
@@ -196,6 +264,7 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
         if (!mbar_wait(empty, ph ^ 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
         uint8_t* st = sm + (kv ? C::kOffV : C::kOffK) + s * C::kKV;
         if (lane == 0) mbar_arrive_expect_tx(full, C::kKV);
+        if (lane == 0 && kv == 0) { WGKV_TRACE(0, j) }
         __syncwarp();
         if (col && !pooled) {
 #pragma unroll
@@ -226,6 +295,7 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
           ok = false;
           break;
         }
+        WGKV_TRACE(1, j)
         if (j > 0 && !mbar_wait(&bar->vfull[ps], ((j - 1) / kStg) & 1)) {
           set_error(p.err, WGKV_ERR_TIMEOUT);
           ok = false;
@@ -238,12 +308,15 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
           if (j > 0) {
             // O_t += P_t(j-1) V(j-1): P sits as packed bf16 pairs in S_t's first 64 columns
             if (!mbar_wait(&bar->pfull[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; break; }
+            WGKV_TRACE(2 + t, j - 1)
             tc_fence_after();
+#ifndef WGKV_EXPERIMENT_NO_PV  // timing experiment only: skips O += P V (wrong results)
 #pragma unroll
             for (int k = 0; k < kKeys / 16; ++k) {
               const uint64_t bb = umma_desc_sw128(vst + k * 2048, C::kBox, 1024);
               umma_ts(tO, tS + k * 8, bb, id_pv, (j > 1 || k > 0) ? 1u : 0u);
             }
+#endif
             umma_commit(&bar->odone[t]);
           }
           if (j < n) {
@@ -264,9 +337,11 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
       }
     }
     __syncwarp();
+  }  // warps 2, 3 of the RW layout: idle until the final barrier
   } else if constexpr (RW) {
     // ====================== softmax: one thread per 128-key row ======================
-    const int sw = warp - 2;
+    if constexpr (kRegSplit) asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
+    const int sw = warp - C::kSoftWarp0;
     const int t = sw >> 2;
     const int quad = warp & 3;                // TMEM lanes 32*quad.. are the ones this warp may access
     const int row = quad * 32 + lane;         // TMEM lane = row of M-tile t
@@ -278,6 +353,7 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < n; ++j) {
       if (ok && !mbar_wait(&bar->sfull[t], j & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
+      if (quad == 0 && lane == 0) { WGKV_TRACE(4 + t, j) }
       tc_fence_after();
       float sv[kKeys];
 #pragma unroll
@@ -293,6 +369,7 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
         lim1 = blk + 1 < nband ? qlim - __ldg(bo_row + blk + 1) : -1;
       }
       tmem_wait_ld();
+      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(8, j) }
       if (lim0 < 63) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) sv[c] = c <= lim0 ? sv[c] : -INFINITY;
@@ -301,10 +378,15 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 64; ++c) sv[64 + c] = c <= lim1 ? sv[64 + c] : -INFINITY;
       }
-      float mraw = -INFINITY;
+      // row max: three-input max, four independent chains
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 4)
-        mraw = fmaxf(mraw, fmaxf(fmaxf(sv[c], sv[c + 1]), fmaxf(sv[c + 2], sv[c + 3])));
+      for (int c = 0; c < kKeys; c += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx[u] = max3(mx[u], sv[c + 2 * u], sv[c + 2 * u + 1]);
+      }
+      const float mraw = max3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(11, j) }
       const float mt = mraw * sc;
       float alpha = 1.f;
       bool need = false;
@@ -314,16 +396,46 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
         m_used = mt;
       }
       const float nbase = m_used == -INFINITY ? 0.f : -m_used;
-      float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pk[kKeys / 2];
+      // p = 2^(s * scale - m): the scale-and-shift as paired FMAs, the exponential on the SFU, the
+      // row sum as paired adds; each 32-key chunk of P goes to TMEM (packed bf16 pairs over the
+      // first S columns) as soon as it is computed
+      const uint64_t sc2 = f2(sc, sc), nb2 = f2(nbase, nbase);
+      uint64_t sa = f2(0.f, 0.f), sb = f2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 2) {
-        const float p0 = fast_exp2(fmaf(sv[c], sc, nbase)), p1 = fast_exp2(fmaf(sv[c + 1], sc, nbase));
-        sum0 += p0;
-        sum1 += p1;
-        pk[c >> 1] = pack_bf16x2(p0, p1);
+      for (int cc = 0; cc < kKeys; cc += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          float x0, x1, x2, x3, p0, p1, p2, p3;
+          const uint64_t xa = fma2(f2(sv[cc + c], sv[cc + c + 1]), sc2, nb2);
+          const uint64_t xb = fma2(f2(sv[cc + c + 2], sv[cc + c + 3]), sc2, nb2);
+          f2_split(xa, x0, x1);
+          f2_split(xb, x2, x3);
+          const int pi = (cc + c) >> 1;  // index of the pair (x0, x1); (x2, x3) is pi + 1
+          if ((pi % WGKV_EMU_PERIOD) < WGKV_EMU_COUNT) {
+            f2_split(exp2_fma2(xa), p0, p1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          if (((pi + 1) % WGKV_EMU_PERIOD) < WGKV_EMU_COUNT) {
+            f2_split(exp2_fma2(xb), p2, p3);
+          } else {
+            p2 = fast_exp2(x2);
+            p3 = fast_exp2(x3);
+          }
+          sa = add2(sa, f2(p0, p1));
+          sb = add2(sb, f2(p2, p3));
+          pk[c >> 1] = pack_bf16x2(p0, p1);
+          pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
+        }
+        tmem_st16(trow + (cc >> 1), pk);
       }
-      l = l * alpha + (sum0 + sum1);
+      float s0, s1, s2, s3;
+      f2_split(sa, s0, s1);
+      f2_split(sb, s2, s3);
+      l = l * alpha + ((s0 + s1) + (s2 + s3));
+      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(12, j) }
       if (j > 0) {
         // PV(j-1) completed before S(j) did (commit order), so O is stable here
         if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
@@ -340,13 +452,14 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
           }
         }
       }
-      // P -> TMEM: the row's 128 keys as 64 packed bf16 pairs over the first S columns
-      tmem_st32(trow, reinterpret_cast<const float*>(pk));
-      tmem_st32(trow + 32, reinterpret_cast<const float*>(pk + 32));
+      // the P stores above and any O rescale must land before the MMA reads them
+      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(9, j) }
       tmem_wait_st();
+      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(10, j) }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->pfull[t]);
+      if (quad == 0 && lane == 0) { WGKV_TRACE(6 + t, j) }
     }
     // ---- epilogue: O / l -> bf16 ----
     if (ok && n > 0) {
@@ -588,3 +701,9 @@ int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_s
 }
 
 }  // namespace wgkv
+
+#ifdef WGKV_EXPERIMENT_TRACE
+extern "C" __attribute__((visibility("default"))) int wgkv_experiment_trace_copy(void* host) {
+  return cudaMemcpyFromSymbol(host, wgkv::g_trace, sizeof(wgkv::g_trace)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -92,7 +92,7 @@ KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_
                     "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1, "wgkv_sparse_prefill_pooled": 1, "wgkv_gather_columns": 1,
                     "wgkv_paged_decode_noalloc": 1, "wgkv_ring_advance": 1, "wgkv_decode_prologue": 1,
                     "wgkv_rms_norm": 1, "wgkv_silu_mul": 1, "wgkv_skinny_gemm": 1, "wgkv_quest_select": 2, "wgkv_argmax": 1,
-                    "wgkv_selftest_wait_limit": 1}
+                    "wgkv_selftest_wait_limit": 1, "wgkv_oproj_allreduce": 1}
 # wgkv_snapkv_evict launches 3 kernels per layer + 1; it is not counted (no benchmark step runs it)
 
 
