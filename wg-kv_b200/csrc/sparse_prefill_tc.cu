@@ -378,14 +378,16 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 64; ++c) sv[64 + c] = c <= lim1 ? sv[64 + c] : -INFINITY;
       }
-      // row max: three-input max, four independent chains
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // row max: three-input max, eight independent chains
+      float mx[8];
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 8) {
+      for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[2 * u], sv[2 * u + 1]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) mx[u] = max3(mx[u], sv[c + 2 * u], sv[c + 2 * u + 1]);
+      for (int c = 16; c < kKeys; c += 16) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[c + 2 * u], sv[c + 2 * u + 1]);
       }
-      const float mraw = max3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(11, j) }
       const float mt = mraw * sc;
       float alpha = 1.f;
@@ -436,11 +438,13 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
       f2_split(sb, s2, s3);
       l = l * alpha + ((s0 + s1) + (s2 + s3));
       if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(12, j) }
-      if (j > 0) {
-        // PV(j-1) completed before S(j) did (commit order), so O is stable here
+      if (j > 0 && __any_sync(0xffffffff, need && alpha != 1.f)) {
+        // O is rescaled only when the running max grew: then wait for PV(j-1) to have landed in O.
+        // (Skipping the wait otherwise is safe: PV_t(j) is issued only after this iteration's P, so
+        // odone[t] is never more than one phase ahead of the parity waited on here or at the end.)
         if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
         tc_fence_after();
-        if (__any_sync(0xffffffff, need && alpha != 1.f)) {
+        {
 #pragma unroll 1
           for (int c0 = 0; c0 < D; c0 += 32) {
             float ov[32];
