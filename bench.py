@@ -746,7 +746,7 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     per_layer = float(((W + glen) * D * 2 * 2).sum()) * 1.02
     resident = int(max(1, min(Ly, 150e9 // per_layer)))
     CFG["layers"] = resident
-    steps_total = args.warmup + K + 8 + 16 + 4  # + the end-to-end and instrumented steps
+    steps_total = args.warmup + K + 40  # + the NCCL comparison, end-to-end and instrumented steps
     cache, rate, glen0 = build_state(dev, steps_total * ((Ly + resident - 1) // resident), seed=2 + 1000 * rank)
     layers = build_layers(dev, rate, seed=3 + 1000 * rank)
     CFG.clear()
@@ -826,6 +826,8 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     for t in tp_layers:
         t.peers = None
     nccl_steps = max(1, min(K, 8))
+    for s in range(2):  # warm-up: cuBLAS heuristics and the first NCCL all-reduce on this stream
+        step(s)
     barrier()
     torch.cuda.synchronize()
     e8, e9 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
