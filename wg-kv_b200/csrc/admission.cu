@@ -310,10 +310,21 @@ __global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs 
   const int64_t ring_row0 = (int64_t(layer) * BH + bh) * P.window;
   uint8_t mk[8];
   int ng = 0, nr = 0;
+  {
+    // the thread's 8 mask bytes: one 8-byte load when they are contiguous and aligned
+    const uint8_t* mp = mv.m + b * mv.sb + h * mv.sh + int64_t(t0) * mv.st;
+    if (mv.st == 1 && t0 + 8 <= L && (reinterpret_cast<uintptr_t>(mp) & 7) == 0) {
+      const uint2 w = *reinterpret_cast<const uint2*>(mp);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mk[j] = uint8_t(((j < 4 ? w.x : w.y) >> (8 * (j & 3))) & 0xff);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mk[j] = t0 + j < L ? mv.at(b, h, t0 + j) : 0;
+    }
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int t = t0 + j;
-    mk[j] = t < L ? mv.at(b, h, t) : 0;
     ng += (t < n_early && mk[j]) ? 1 : 0;
     nr += (t < L && t >= ring_start) ? 1 : 0;
   }
@@ -342,6 +353,45 @@ __global__ void __launch_bounds__(kScanThreads) prefill_scatter_kernel(PoolArgs 
   const int n = s_n;
   // copy rows: one warp-quarter (8 lanes) per row
   const int grp = threadIdx.x >> 3, gl = threadIdx.x & 7;
+  if (kVec16 && D <= 128 && !(P.local_pre_key && PK.p)) {
+    // two rows per group per pass, every load issued before any store: 8 x 16 B in flight per lane
+    constexpr int kG = kScanThreads / 8;
+    const int nv = D / 8;  // 16-byte vectors per row (8 or 16)
+    for (int e0 = grp; e0 < n; e0 += 2 * kG) {
+      uint4 kr[2][2], vr[2][2];
+      int64_t dst[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int e = e0 + u * kG;
+        if (e >= n) continue;
+        const int t = list[e].x;
+        dst[u] = e >= tot ? ring_row0 + (-2 - list[e].y) : gdst0 + e;
+        const uint16_t* ks = K.p + b * K.sb + h * K.sh + int64_t(t) * K.st;
+        const uint16_t* vs = V.p + b * V.sb + h * V.sh + int64_t(t) * V.st;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int c = gl + 8 * i;
+          if (c < nv) {
+            kr[u][i] = __ldg(reinterpret_cast<const uint4*>(ks) + c);
+            vr[u][i] = __ldg(reinterpret_cast<const uint4*>(vs) + c);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (e0 + u * kG >= n) continue;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int c = gl + 8 * i;
+          if (c < nv) {
+            reinterpret_cast<uint4*>(P.k + dst[u] * D)[c] = kr[u][i];
+            reinterpret_cast<uint4*>(P.v + dst[u] * D)[c] = vr[u][i];
+          }
+        }
+      }
+    }
+    return;
+  }
   for (int e = grp; e < n; e += kScanThreads / 8) {
     const int t = list[e].x;
     int64_t dst;

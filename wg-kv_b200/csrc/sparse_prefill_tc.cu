@@ -36,7 +36,7 @@ constexpr int kKeys = 128;  // keys per K/V tile (two 64-key halves)
 constexpr int kStg = 2;     // K and V stages
 constexpr float kRescaleThreshold = 8.f;  // log2 of the largest tolerated growth of unnormalised terms
 
-template <int D, int NM, bool RW = false>
+template <int D, int NM, int HV>
 struct Tc {
   static constexpr int kDB = D / 64;                 // 64-column boxes per row
   static constexpr int kQTile = kDB * 16384;         // one M-tile of Q: kDB boxes x 128 rows x 128 B
@@ -47,13 +47,16 @@ struct Tc {
   static constexpr int kOffBar = kOffV + kStg * kKV;
   static constexpr int kOffX = kOffBar + 512;        // row-max / row-sum exchange [3][NM][2][128] floats
   static constexpr int kSmem = kOffX + 3 * NM * 2 * 128 * 4 + 1024;  // + alignment slack
-  // producer, MMA, then per M-tile two softmax warpgroups (one per 64-key half) or, with RW, a
-  // first warpgroup (producer, MMA, two idle warps) and one warpgroup per M-tile whose threads each
-  // own a whole 128-key row
-  static constexpr int kThreads = RW ? 128 + 128 * NM : 64 + 256 * NM;
-  static constexpr int kSoftWarp0 = RW ? 4 : 2;      // first softmax warp
-  static constexpr int kSoftWarps = RW ? 4 : 8;      // softmax warps per M-tile
+  // warpgroup 0: producer, MMA issuer, two idle warps; then per M-tile HV softmax warpgroups, the
+  // threads of a row splitting its 128 keys HV ways
+  static constexpr int kThreads = 128 + 128 * NM * HV;
+  static constexpr int kSoftWarps = 4 * HV;          // softmax warps per M-tile
   static constexpr int kTmemCols = NM == 2 ? 512 : 256;
+  // register split (setmaxnreg) between warpgroup 0 and the softmax warpgroups, within the launch's
+  // threads x registers: 384 threads launch at 168 (128 x 56 + 256 x 224), 640 at 96 (128 x 64 + 512 x 104)
+  static constexpr int kRegLo = kThreads == 640 ? 64 : 56;
+  static constexpr int kRegHi = kThreads == 640 ? 104 : 224;
+  static constexpr bool kRegSplit = kThreads > 256;
 };
 
 // 2^x on the SFU (ex2.approx, flush-to-zero): the softmax terms are rounded to
@@ -148,13 +151,13 @@ struct Bars {
   uint32_t tmem;
 };
 
-template <int D, int NM, bool POOL, bool RW>
-__global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
+template <int D, int NM, bool POOL, int HV>
+__global__ void __launch_bounds__(Tc<D, NM, HV>::kThreads, 1)
     sparse_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKg,
                              const __grid_constant__ CUtensorMap tmVg, const __grid_constant__ CUtensorMap tmKp,
                              const __grid_constant__ CUtensorMap tmVp, TcParams p) {
-  using C = Tc<D, NM, RW>;
+  using C = Tc<D, NM, HV>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bar = reinterpret_cast<Bars*>(sm + C::kOffBar);
@@ -194,11 +197,8 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem;
   bool ok = true;
-  // RW with two M-tiles: 384 threads launched at 168 registers; the first warpgroup (producer, MMA)
-  // gives registers up to the two softmax warpgroups (128 x 56 + 256 x 224 = 384 x 168)
-  constexpr bool kRegSplit = RW && NM == 2;
-  if (warp < C::kSoftWarp0) {
-  if constexpr (kRegSplit) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+  if (warp < 4) {
+  if constexpr (C::kRegSplit) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::kRegLo));
   if (warp == 0) {
     // ================================ producer ================================
     if (lane == 0) {
@@ -337,58 +337,73 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
       }
     }
     __syncwarp();
-  }  // warps 2, 3 of the RW layout: idle until the final barrier
-  } else if constexpr (RW) {
-    // ====================== softmax: one thread per 128-key row ======================
-    if constexpr (kRegSplit) asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
-    const int sw = warp - C::kSoftWarp0;
-    const int t = sw >> 2;
+  }  // warps 2, 3: idle until the final barrier
+  } else {
+    // ====================== softmax: HV threads per 128-key row ======================
+    if constexpr (C::kRegSplit) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::kRegHi));
+    constexpr int KPT = kKeys / HV;           // keys of a row this thread owns
+    constexpr int kOC = D / HV;               // O columns this thread owns
+    const int sw = warp - 4;
+    const int t = sw / (4 * HV);
+    const int hf = (sw >> 2) % HV;            // which KPT-key slice of every tile
     const int quad = warp & 3;                // TMEM lanes 32*quad.. are the ones this warp may access
     const int row = quad * 32 + lane;         // TMEM lane = row of M-tile t
     const int hh = 2 * t + (row >> 6);
     const int q = s0 + (row & 63);
+    const int bar_id = 1 + t * 4 + quad;      // named barrier of the HV warps sharing these rows
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
+    float* xm = reinterpret_cast<float*>(sm + C::kOffX);  // [slot][t][hf][row]
+    auto xslot = [&](int slot, int h_) { return xm + ((slot * NM + t) * 2 + h_) * 128 + row; };
     const float sc = p.scale_log2;
     const int qlim = min(q, p.L - 1);
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < n; ++j) {
       if (ok && !mbar_wait(&bar->sfull[t], j & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
-      if (quad == 0 && lane == 0) { WGKV_TRACE(4 + t, j) }
+      if (quad == 0 && lane == 0 && hf == 0) { WGKV_TRACE(4 + t, j) }
       tc_fence_after();
-      float sv[kKeys];
+      float sv[KPT];
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 32) tmem_ld32(trow + c, sv + c);
-      // limits of the two 64-key halves (column tail / causal band / missing band block)
-      int lim0, lim1;
-      if (j < ntc) {
-        lim0 = ncol - j * kKeys - 1;
-        lim1 = lim0 - 64;
-      } else {
-        const int blk = 2 * (j - ntc);
-        lim0 = blk < nband ? qlim - __ldg(bo_row + blk) : -1;
-        lim1 = blk + 1 < nband ? qlim - __ldg(bo_row + blk + 1) : -1;
+      for (int c = 0; c < KPT; c += 32) tmem_ld32(trow + hf * KPT + c, sv + c);
+      // limits of this thread's 64-key blocks (column tail / causal band / missing band block)
+      int lim[KPT / 64];
+#pragma unroll
+      for (int u = 0; u < KPT / 64; ++u) {
+        const int kb = hf * (KPT / 64) + u;   // 64-key block of the tile
+        if (j < ntc) {
+          lim[u] = ncol - j * kKeys - kb * 64 - 1;
+        } else {
+          const int blk = 2 * (j - ntc) + kb;
+          lim[u] = blk < nband ? qlim - __ldg(bo_row + blk) : -1;
+        }
       }
       tmem_wait_ld();
-      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(8, j) }
-      if (lim0 < 63) {
+      if (quad == 0 && lane == 0 && t == 0 && hf == 0) { WGKV_TRACE(8, j) }
 #pragma unroll
-        for (int c = 0; c < 64; ++c) sv[c] = c <= lim0 ? sv[c] : -INFINITY;
+      for (int u = 0; u < KPT / 64; ++u) {
+        if (lim[u] < 63) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) sv[u * 64 + c] = c <= lim[u] ? sv[u * 64 + c] : -INFINITY;
+        }
       }
-      if (lim1 < 63) {
+      // row max: three-input max over independent chains
+      constexpr int kCh = KPT / 16;           // 8 chains (128 keys) or 4 (64 keys)
+      float mx[kCh];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) sv[64 + c] = c <= lim1 ? sv[64 + c] : -INFINITY;
+      for (int u = 0; u < kCh; ++u) mx[u] = fmaxf(sv[2 * u], sv[2 * u + 1]);
+#pragma unroll
+      for (int c = 2 * kCh; c < KPT; c += 2 * kCh) {
+#pragma unroll
+        for (int u = 0; u < kCh; ++u) mx[u] = max3(mx[u], sv[c + 2 * u], sv[c + 2 * u + 1]);
       }
-      // row max: three-input max, eight independent chains
-      float mx[8];
+      float mraw = mx[0];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx[u] = fmaxf(sv[2 * u], sv[2 * u + 1]);
-#pragma unroll
-      for (int c = 16; c < kKeys; c += 16) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], sv[c + 2 * u], sv[c + 2 * u + 1]);
+      for (int u = 1; u < kCh; ++u) mraw = fmaxf(mraw, mx[u]);
+      if constexpr (HV == 2) {
+        *xslot(j & 1, hf) = mraw;
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");  // both slices have their tile max
+        mraw = fmaxf(mraw, *xslot(j & 1, hf ^ 1));
       }
-      const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(11, j) }
+      if (quad == 0 && lane == 0 && t == 0 && hf == 0) { WGKV_TRACE(11, j) }
       const float mt = mraw * sc;
       float alpha = 1.f;
       bool need = false;
@@ -397,14 +412,30 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
         alpha = exp2f(m_used - mt);  // 0 when m_used = -inf
         m_used = mt;
       }
+      if (j > 0 && __any_sync(0xffffffff, need && alpha != 1.f)) {
+        // O is rescaled only when the running max grew: then wait for PV(j-1) to have landed in O.
+        // (Skipping the wait otherwise is safe: PV_t(j) is issued only after this iteration's P, so
+        // odone[t] is never more than one phase ahead of the parity waited on here or at the end.)
+        if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < kOC; c0 += 32) {
+          float ov[32];
+          tmem_ld32(trow + 128 + hf * kOC + c0, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) ov[c] *= alpha;
+          tmem_st32(trow + 128 + hf * kOC + c0, ov);
+        }
+      }
       const float nbase = m_used == -INFINITY ? 0.f : -m_used;
-      // p = 2^(s * scale - m): the scale-and-shift as paired FMAs, the exponential on the SFU, the
-      // row sum as paired adds; each 32-key chunk of P goes to TMEM (packed bf16 pairs over the
-      // first S columns) as soon as it is computed
+      // p = 2^(s * scale - m): the scale-and-shift as paired FMAs, the exponential on the SFU (part
+      // on the FMA pipe), the row sum as paired adds; each 32-key chunk of P goes to TMEM (packed
+      // bf16 pairs over the first S columns) as soon as it is computed
       const uint64_t sc2 = f2(sc, sc), nb2 = f2(nbase, nbase);
       uint64_t sa = f2(0.f, 0.f), sb = f2(0.f, 0.f);
 #pragma unroll
-      for (int cc = 0; cc < kKeys; cc += 32) {
+      for (int cc = 0; cc < KPT; cc += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 4) {
@@ -431,171 +462,37 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
           pk[c >> 1] = pack_bf16x2(p0, p1);
           pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
         }
-        tmem_st16(trow + (cc >> 1), pk);
+        tmem_st16(trow + ((hf * KPT + cc) >> 1), pk);
       }
-      float s0, s1, s2, s3;
-      f2_split(sa, s0, s1);
-      f2_split(sb, s2, s3);
-      l = l * alpha + ((s0 + s1) + (s2 + s3));
-      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(12, j) }
-      if (j > 0 && __any_sync(0xffffffff, need && alpha != 1.f)) {
-        // O is rescaled only when the running max grew: then wait for PV(j-1) to have landed in O.
-        // (Skipping the wait otherwise is safe: PV_t(j) is issued only after this iteration's P, so
-        // odone[t] is never more than one phase ahead of the parity waited on here or at the end.)
-        if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
-        tc_fence_after();
-        {
-#pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 32) {
-            float ov[32];
-            tmem_ld32(trow + 128 + c0, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) ov[c] *= alpha;
-            tmem_st32(trow + 128 + c0, ov);
-          }
-        }
-      }
-      // the P stores above and any O rescale must land before the MMA reads them
-      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(9, j) }
+      float s0_, s1_, s2_, s3_;
+      f2_split(sa, s0_, s1_);
+      f2_split(sb, s2_, s3_);
+      l = l * alpha + ((s0_ + s1_) + (s2_ + s3_));
+      if (quad == 0 && lane == 0 && t == 0 && hf == 0) { WGKV_TRACE(12, j) }
+      // the P stores and any O rescale must land before the MMA reads them
       tmem_wait_st();
-      if (quad == 0 && lane == 0 && t == 0) { WGKV_TRACE(10, j) }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->pfull[t]);
-      if (quad == 0 && lane == 0) { WGKV_TRACE(6 + t, j) }
+      if (quad == 0 && lane == 0 && hf == 0) { WGKV_TRACE(6 + t, j) }
     }
     // ---- epilogue: O / l -> bf16 ----
     if (ok && n > 0) {
       if (!mbar_wait(&bar->odone[t], (n - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
     }
     tc_fence_after();
+    if constexpr (HV == 2) {
+      *xslot(2, hf) = l;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      l += *xslot(2, hf ^ 1);
+    }
     const bool any = l > 0.f;  // a row that saw no key (degenerate index sets only) writes zeros
     const float inv = any ? 1.f / l : 0.f;
-    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh;
-#pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      float ov[32];
-      tmem_ld32(trow + 128 + c0, ov);
-      tmem_wait_ld();
-      if (ok && q < p.L) {
-        if (!any) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = 0.f;
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          uint4 v;
-          v.x = pack_bf16x2(ov[c] * inv, ov[c + 1] * inv);
-          v.y = pack_bf16x2(ov[c + 2] * inv, ov[c + 3] * inv);
-          v.z = pack_bf16x2(ov[c + 4] * inv, ov[c + 5] * inv);
-          v.w = pack_bf16x2(ov[c + 6] * inv, ov[c + 7] * inv);
-          *reinterpret_cast<uint4*>(orow + c0 + c) = v;
-        }
-      }
-    }
-  } else {
-    // ============================ softmax warpgroups ============================
-    const int sw = warp - 2;
-    const int t = sw >> 3;
-    const int half = (sw >> 2) & 1;           // 64-key half of every tile
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;         // TMEM lane = row of M-tile t
-    const int hh = 2 * t + (row >> 6);
-    const int q = s0 + (row & 63);
-    const int bar_id = 1 + t * 4 + quad;       // named barrier of the two warps sharing these rows
-    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
-    float* xm = reinterpret_cast<float*>(sm + C::kOffX);  // [slot][t][half][row]
-    auto xslot = [&](int slot, int hf) { return xm + ((slot * NM + t) * 2 + hf) * 128 + row; };
-    const float sc = p.scale_log2;
-    constexpr int kOC = D / 2;                 // O columns of this warpgroup
-    float m_used = -INFINITY, l = 0.f;
-    for (int j = 0; j < n; ++j) {
-      if (ok && !mbar_wait(&bar->sfull[t], j & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
-      tc_fence_after();
-      float sv[64];
-      tmem_ld32(trow + half * 64, sv);
-      tmem_ld32(trow + half * 64 + 32, sv + 32);
-      tmem_wait_ld();
-      // mask (raw scores; the positive scale is applied inside the exponent) + tile max
-      float mraw = -INFINITY;
-      int lim;
-      if (j < ntc) {
-        lim = ncol - j * kKeys - half * 64 - 1;  // column tail
-      } else {
-        const int blk = 2 * (j - ntc) + half;
-        lim = blk < nband ? min(q, p.L - 1) - __ldg(bo_row + blk) : -1;  // causal band / missing block
-      }
-      if (lim >= 63) {
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) mraw = fmaxf(mraw, fmaxf(sv[c], sv[c + 1]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          sv[c] = c <= lim ? sv[c] : -INFINITY;
-          mraw = fmaxf(mraw, sv[c]);
-        }
-      }
-      *xslot(j & 1, half) = mraw;
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");  // both halves have read S_t
-      mraw = fmaxf(mraw, *xslot(j & 1, half ^ 1));
-      const float mt = mraw * sc;
-      float alpha = 1.f;
-      bool need = false;
-      if (mt > m_used + kRescaleThreshold) {  // also true on the first visible key (m_used = -inf)
-        need = true;
-        alpha = exp2f(m_used - mt);  // 0 when m_used = -inf
-        m_used = mt;
-      }
-      const float nbase = m_used == -INFINITY ? 0.f : -m_used;
-      float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pk[32];
-#pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = fast_exp2(fmaf(sv[c], sc, nbase)), p1 = fast_exp2(fmaf(sv[c + 1], sc, nbase));
-        sum0 += p0;
-        sum1 += p1;
-        pk[c >> 1] = pack_bf16x2(p0, p1);
-      }
-      l = l * alpha + (sum0 + sum1);
-      if (j > 0) {
-        // PV(j-1) completed before S(j) did (commit order), so O is stable here
-        if (ok && !mbar_wait(&bar->odone[t], (j - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
-        tc_fence_after();
-        if (__any_sync(0xffffffff, need && alpha != 1.f)) {
-#pragma unroll 1
-          for (int c0 = 0; c0 < kOC; c0 += 32) {
-            float ov[32];
-            tmem_ld32(trow + 128 + half * kOC + c0, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) ov[c] *= alpha;
-            tmem_st32(trow + 128 + half * kOC + c0, ov);
-          }
-        }
-      }
-      // P -> TMEM: keys 64*half .. +63 as 32 packed columns over S columns both halves have read
-      tmem_st32(trow + half * 32, reinterpret_cast<const float*>(pk));
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->pfull[t]);
-    }
-    // ---- epilogue: O / l -> bf16 ----
-    if (ok && n > 0) {
-      if (!mbar_wait(&bar->odone[t], (n - 1) & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
-    }
-    tc_fence_after();
-    *xslot(2, half) = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    l += *xslot(2, half ^ 1);
-    const bool any = l > 0.f;  // a row that saw no key (degenerate index sets only) writes zeros
-    const float inv = any ? 1.f / l : 0.f;
-    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh + half * kOC;
+    uint16_t* orow = p.out + b * p.o_sb + int64_t(q) * p.o_sl + int64_t(hq0 + hh) * p.o_sh + hf * kOC;
 #pragma unroll 1
     for (int c0 = 0; c0 < kOC; c0 += 32) {
       float ov[32];
-      tmem_ld32(trow + 128 + half * kOC + c0, ov);
+      tmem_ld32(trow + 128 + hf * kOC + c0, ov);
       tmem_wait_ld();
       if (ok && q < p.L) {
         if (!any) {
@@ -622,11 +519,11 @@ __global__ void __launch_bounds__(Tc<D, NM, RW>::kThreads, 1)
   }
 }
 
-template <int D, int NM, bool POOL, bool RW>
+template <int D, int NM, bool POOL, int HV>
 int launch_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q_sl, int64_t k_sl, int64_t v_sl,
               int Hq, int Hk, const uint16_t* pool_k, const uint16_t* pool_v, int64_t pool_rows, const TcParams& p,
               cudaStream_t stream) {
-  using C = Tc<D, NM, RW>;
+  using C = Tc<D, NM, HV>;
   CUtensorMap mq, mk, mv, mkg, mvg;
   const uint64_t rows = uint64_t(p.B) * p.L;
   if (!encode_2d_bf16(&mq, q, uint64_t(Hq) * D, rows, q_sl, 64, 64, true)) return WGKV_ECUDA;
@@ -643,13 +540,13 @@ int launch_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t q
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(sparse_prefill_tc_kernel<D, NM, POOL, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(sparse_prefill_tc_kernel<D, NM, POOL, HV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmem) != cudaSuccess)
       return WGKV_ECUDA;
     attr[dev] = true;
   }
   dim3 grid(p.R, p.Hk * p.n_hg, p.B);
-  sparse_prefill_tc_kernel<D, NM, POOL, RW><<<grid, C::kThreads, C::kSmem, stream>>>(mq, mk, mv, mkg, mvg, mkp, mvp, p);
+  sparse_prefill_tc_kernel<D, NM, POOL, HV><<<grid, C::kThreads, C::kSmem, stream>>>(mq, mk, mv, mkg, mvg, mkp, mvp, p);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -684,16 +581,16 @@ int sparse_prefill_tc(const uint16_t* q, int64_t q_sb, int64_t q_sl, int64_t q_s
   const bool pool = pool_k != nullptr;
   if (pool && (!pool_v || !table || ((reinterpret_cast<uintptr_t>(pool_k) | reinterpret_cast<uintptr_t>(pool_v)) & 15)))
     return WGKV_EINVAL;
-  // one softmax thread per 128-key row (default; 3-4 % faster at the C3 shape) or two per row
-  // (WGKV_PREFILL_ROWWISE=0)
-  static const bool rw = [] {
-    const char* e = getenv("WGKV_PREFILL_ROWWISE");
-    return !(e && e[0] == '0');
+  // threads per 128-key row of the softmax: 1 (default; 8-10 % faster than 2 at the C3 shape) or
+  // 2 (WGKV_PREFILL_SPLIT=2)
+  static const int hv = [] {
+    const char* e = getenv("WGKV_PREFILL_SPLIT");
+    return (e && e[0] == '2') ? 2 : 1;
   }();
-#define WGKV_TC_LAUNCH2(DD, NMM, RWW)                                                                            \
-  (pool ? launch_tc<DD, NMM, true, RWW>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream) \
-        : launch_tc<DD, NMM, false, RWW>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream))
-#define WGKV_TC_LAUNCH(DD, NMM) (rw ? WGKV_TC_LAUNCH2(DD, NMM, true) : WGKV_TC_LAUNCH2(DD, NMM, false))
+#define WGKV_TC_LAUNCH2(DD, NMM, HVV)                                                                            \
+  (pool ? launch_tc<DD, NMM, true, HVV>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream) \
+        : launch_tc<DD, NMM, false, HVV>(q, k, v, q_sl, k_sl, v_sl, Hq, Hk, pool_k, pool_v, pool_rows, p, stream))
+#define WGKV_TC_LAUNCH(DD, NMM) (hv == 1 ? WGKV_TC_LAUNCH2(DD, NMM, 1) : WGKV_TC_LAUNCH2(DD, NMM, 2))
   if (G % 4 == 0) {
     p.n_hg = G / 4;
     return D == 128 ? WGKV_TC_LAUNCH(128, 2) : WGKV_TC_LAUNCH(64, 2);
