@@ -4,7 +4,8 @@ Each rank runs in its own process on its own GPU (NCCL process group for the hos
 exchange and the comparison).  Every call's output must equal the unfused path -- the same GEMM
 rounded to bf16 on each rank, then an NCCL all-reduce -- within 2e-2 abs / 1e-2 rel, and be
 bit-identical on every rank; consecutive calls (alternating buffer parities, several row counts)
-must not interfere.  Skipped when fewer than 2 GPUs are visible."""
+must not interfere.  A last call made by rank 0 alone must end with WGKV_ERR_TIMEOUT (its peers
+never publish) and leave the GPU usable.  Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -55,8 +56,25 @@ def _worker(rank, world, port, out_q):
             same = same and all(torch.equal(gathered[0], t) for t in gathered)
         dist.barrier()
         torch.cuda.synchronize()
+        # a call that only rank 0 makes: its peers never publish, so its bounded waits run out and
+        # it reports WGKV_ERR_TIMEOUT instead of hanging (no GPU fault involved)
+        timed_out = None
+        if rank == 0:
+            a = torch.randn(8, k, device="cuda").bfloat16()
+            w = torch.randn(n_out, k, device="cuda").bfloat16()
+            y = torch.empty(8, n_out, dtype=torch.bfloat16, device="cuda")
+            peers.oproj_allreduce(a, w, y)
+            torch.cuda.synchronize()
+            try:
+                wgkv.check_errors()
+                timed_out = False
+            except AssertionError:
+                timed_out = True
+            torch.zeros(1, device="cuda").add_(1)  # the context is still usable
+            torch.cuda.synchronize()
+        dist.barrier()
         peers.close()
-        out_q.put((rank, True, same, worst))
+        out_q.put((rank, True, same, worst if rank else (worst, timed_out)))
     except Exception as e:  # reported to the parent
         out_q.put((rank, False, False, repr(e)))
     finally:
@@ -77,4 +95,5 @@ def test_fused_oproj_allreduce_matches_gemm_plus_nccl():
         p.join(timeout=60)
     assert all(r[1] for r in res), res
     assert all(r[2] for r in res), "ranks disagree"
+    assert res[0][3][1] is True, "the unmatched call did not report a timeout"
     assert all(p.exitcode == 0 for p in procs)

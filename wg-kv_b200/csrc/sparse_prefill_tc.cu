@@ -53,9 +53,9 @@ struct Tc {
   static constexpr int kSoftWarps = 4 * HV;          // softmax warps per M-tile
   static constexpr int kTmemCols = NM == 2 ? 512 : 256;
   // register split (setmaxnreg) between warpgroup 0 and the softmax warpgroups, within the launch's
-  // threads x registers: 384 threads launch at 168 (128 x 56 + 256 x 224), 640 at 96 (128 x 64 + 512 x 104)
-  static constexpr int kRegLo = kThreads == 640 ? 64 : 56;
-  static constexpr int kRegHi = kThreads == 640 ? 104 : 224;
+  // threads x registers: 384 threads launch at 168 (128 x 64 + 256 x 216), 640 at 96 (128 x 64 + 512 x 104)
+  static constexpr int kRegLo = 64;
+  static constexpr int kRegHi = kThreads == 640 ? 104 : 216;
   static constexpr bool kRegSplit = kThreads > 256;
 };
 
