@@ -3,7 +3,8 @@
  *
  * Every entry point takes plain device pointers, sizes and element strides,
  * plus a CUDA stream passed as `void*` (a cudaStream_t; NULL = legacy default
- * stream).  Nothing here allocates device memory, synchronises the device or
+ * stream).  Nothing here allocates device memory, synchronises the device (apart from the one-time
+ * table build of wgkv_gate_scores, noted there) or
  * reads device data back to the host: capacity violations detected on the
  * device are OR-ed into the caller's device error word `err` (WGKV_ERR_*),
  * which the caller inspects when it chooses to synchronise.  Host-detectable
@@ -144,7 +145,9 @@ typedef struct wgkv_pool {
  * einsum fast path (:185-196: products rounded, then the bias added and rounded; score_floor unused).
  * Inputs are (B, Hk, L, D) with element strides (sb, sh, st); unused inputs may be NULL.  w1
  * (Hk, inner, I), b1 (Hk, inner), w2 (Hk, inner), b2 (Hk) bf16.  Either output may be NULL; strides
- * are in elements.
+ * are in elements.  The first call on a device made outside stream capture builds a 16 KB table of
+ * the activation on that device (one launch on `stream`, waited for); calls before that compute the
+ * activation directly, with identical results.
  * Constraints: D in {64, 128}; inner % 8 == 0; I = D * popcount(input_mask) <= 384.
  */
 WGKV_API int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,
@@ -282,7 +285,7 @@ WGKV_API int wgkv_ipc_close(void* base);
  * columns in rank order (fp32), so every GPU gets identical bits.  Every rank must make the same
  * sequence of calls (same rows, n_out) on its own stream; with world == 1 it is the plain GEMM.
  * Waits on peers are bounded (~2 s): a peer that never arrives sets WGKV_ERR_TIMEOUT in err and the
- * call completes with undefined y.  k % 64 == 0, n_out % 32 == 0, n_out / 32 <= the SM count,
+ * call completes with undefined y.  k % 128 == 0, n_out % 32 == 0, n_out / 32 <= the SM count,
  * rows <= max_rows, 16-byte aligned rows.
  */
 WGKV_API int wgkv_oproj_allreduce(const uint16_t* a, int64_t lda, int rows, int k, const uint16_t* w, int n_out,

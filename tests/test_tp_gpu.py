@@ -81,7 +81,7 @@ def test_fused_oproj_group_of_one_is_the_gemm(rows, k):
     peers = PeerGroup(max_rows=256, max_cols=n_out)
     y = torch.empty(rows, n_out, dtype=torch.bfloat16, device="cuda")
     for _ in range(3):  # repeated calls advance the device epoch
-        peers.oproj_allreduce(a, w, y)
+        peers.oproj_allreduce(a, w, y, kernel=True)
     torch.cuda.synchronize()
     import wgkv
     wgkv.check_errors()

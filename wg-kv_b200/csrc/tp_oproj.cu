@@ -31,10 +31,12 @@ namespace {
 
 constexpr int kTpCols = 32;          // output columns per CTA
 constexpr int kTpRows = 64;          // rows per m-block (4 warps x 16)
-constexpr int kTpK = 64;             // K per pipeline stage
-constexpr int kTpStages = 3;
+constexpr int kTpK = 128;            // K per pipeline stage
+constexpr int kTpStages = 4;
 constexpr int kTpThreads = 128;
 constexpr int kTpRS = kTpK + 8;      // padded smem row (elements): conflict-free ldmatrix
+constexpr int kTpStageElems = (kTpRows + kTpCols) * kTpRS;
+constexpr size_t kTpSmem = size_t(kTpStages) * kTpStageElems * 2;  // 104 KB, dynamic
 
 struct TpArgs {
   const uint16_t* a;
@@ -81,8 +83,9 @@ WGKV_DEV uint32_t* flag_at(uint32_t* base, int parity, int src, int tile, int st
 }
 
 __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(TpArgs p) {
-  __shared__ __align__(128) uint16_t as[kTpStages][kTpRows * kTpRS];
-  __shared__ __align__(128) uint16_t ws[kTpStages][kTpCols * kTpRS];
+  extern __shared__ __align__(128) uint16_t tp_smem[];
+  auto as = [&](int st) { return tp_smem + st * kTpStageElems; };
+  auto ws = [&](int st) { return tp_smem + st * kTpStageElems + kTpRows * kTpRS; };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, n_tiles = gridDim.x;
   const int fstride = p.g.max_cols / kTpCols + 1;
@@ -101,18 +104,18 @@ __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(TpArgs p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     auto load = [&](int kc, int st) {
-      // A: 64 rows x 64 k = 512 vectors of 16 B; W: 32 rows x 64 k = 256 vectors
+      // A: 64 rows x 128 k = 1024 vectors of 16 B; W: 32 rows x 128 k = 512 vectors
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int v = tid + i * kTpThreads, r = v >> 3, c = (v & 7) * 8;
+      for (int i = 0; i < 8; ++i) {
+        const int v = tid + i * kTpThreads, r = v >> 4, c = (v & 15) * 8;
         const bool ok = m0 + r < p.rows;
         const uint16_t* src = p.a + int64_t(ok ? m0 + r : 0) * p.lda + kc * kTpK + c;
-        cp_async16(smem_u32(&as[st][r * kTpRS + c]), src, ok);
+        cp_async16(smem_u32(as(st) + r * kTpRS + c), src, ok);
       }
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int v = tid + i * kTpThreads, r = v >> 3, c = (v & 7) * 8;
-        cp_async16(smem_u32(&ws[st][r * kTpRS + c]), p.w + int64_t(c0 + r) * p.k + kc * kTpK + c, true);
+      for (int i = 0; i < 4; ++i) {
+        const int v = tid + i * kTpThreads, r = v >> 4, c = (v & 15) * 8;
+        cp_async16(smem_u32(ws(st) + r * kTpRS + c), p.w + int64_t(c0 + r) * p.k + kc * kTpK + c, true);
       }
     };
 #pragma unroll
@@ -126,8 +129,8 @@ __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(TpArgs p) {
       if (kc + kTpStages - 1 < nk) load(kc + kTpStages - 1, (kc + kTpStages - 1) % kTpStages);
       cp_async_commit();
       const int st = kc % kTpStages;
-      const uint32_t abase = smem_u32(&as[st][(warp * 16 + (mi & 1) * 8 + ri) * kTpRS + (mi >> 1) * 8]);
-      const uint32_t wbase = smem_u32(&ws[st][((mi >> 1) * 8 + ri) * kTpRS + (mi & 1) * 8]);
+      const uint32_t abase = smem_u32(as(st) + (warp * 16 + (mi & 1) * 8 + ri) * kTpRS + (mi >> 1) * 8);
+      const uint32_t wbase = smem_u32(ws(st) + ((mi >> 1) * 8 + ri) * kTpRS + (mi & 1) * 8);
 #pragma unroll
       for (int kk = 0; kk < kTpK / 16; ++kk) {
         uint32_t a[4];
@@ -279,6 +282,15 @@ extern "C" int wgkv_oproj_allreduce(const uint16_t* a, int64_t lda, int rows, in
   const wgkv_peer_group& g = *group;
   if (g.world < 1 || g.world > WGKV_TP_MAX_WORLD || g.rank < 0 || g.rank >= g.world) return WGKV_EINVAL;
   if (k % kTpK || n_out % kTpCols || lda < k || ldy < n_out || lda % 8 || ldy % 8) return WGKV_EINVAL;
+  static bool attr[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return WGKV_ECUDA;
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(oproj_allreduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTpSmem)) !=
+        cudaSuccess)
+      return WGKV_ECUDA;
+    attr[dev] = true;
+  }
   if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15))
     return WGKV_EINVAL;
   const int sms = device_sms();
@@ -290,6 +302,6 @@ extern "C" int wgkv_oproj_allreduce(const uint16_t* a, int64_t lda, int rows, in
       if (!g.partial[r] || !g.flags[r] || (reinterpret_cast<uintptr_t>(g.partial[r]) & 15)) return WGKV_EINVAL;
   }
   TpArgs p{a, lda, rows, k, w, n_out, y, ldy, g, err};
-  oproj_allreduce_kernel<<<n_out / kTpCols, kTpThreads, 0, as_stream(stream)>>>(p);
+  oproj_allreduce_kernel<<<n_out / kTpCols, kTpThreads, kTpSmem, as_stream(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

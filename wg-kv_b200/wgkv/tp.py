@@ -110,9 +110,14 @@ class PeerGroup:
             _ipc_release(hr)
         self._handles = []
 
-    def oproj_allreduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor):
-        """out (rows, n_out) = sum over the group of a (rows, k) @ w (n_out, k)^T (``wgkv_oproj_allreduce``)."""
+    def oproj_allreduce(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, kernel: bool = False):
+        """out (rows, n_out) = sum over the group of a (rows, k) @ w (n_out, k)^T (``wgkv_oproj_allreduce``).
+
+        In a group of one there is nothing to sum and the product is cuBLAS's GEMM unless ``kernel``
+        asks for the fused kernel (which then computes the same GEMM)."""
         assert a.dtype == w.dtype == out.dtype == torch.bfloat16 and a.stride(1) == 1 and out.stride(1) == 1
+        if self.world == 1 and not kernel:
+            return torch.matmul(a, w.t(), out=out)
         w = w if w.is_contiguous() else w.contiguous()
         check(lib.wgkv_oproj_allreduce(a.data_ptr(), a.stride(0), a.shape[0], a.shape[1], w.data_ptr(), w.shape[0],
                                        out.data_ptr(), out.stride(0), ctypes.byref(self.struct),
