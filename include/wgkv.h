@@ -3,8 +3,7 @@
  *
  * Every entry point takes plain device pointers, sizes and element strides,
  * plus a CUDA stream passed as `void*` (a cudaStream_t; NULL = legacy default
- * stream).  Nothing here allocates device memory, synchronises the device (apart from the one-time
- * table build of wgkv_gate_scores, noted there) or
+ * stream).  Nothing here allocates device memory, synchronises the device or
  * reads device data back to the host: capacity violations detected on the
  * device are OR-ed into the caller's device error word `err` (WGKV_ERR_*),
  * which the caller inspects when it chooses to synchronise.  Host-detectable
@@ -145,9 +144,7 @@ typedef struct wgkv_pool {
  * einsum fast path (:185-196: products rounded, then the bias added and rounded; score_floor unused).
  * Inputs are (B, Hk, L, D) with element strides (sb, sh, st); unused inputs may be NULL.  w1
  * (Hk, inner, I), b1 (Hk, inner), w2 (Hk, inner), b2 (Hk) bf16.  Either output may be NULL; strides
- * are in elements.  The first call on a device made outside stream capture builds a 16 KB table of
- * the activation on that device (one launch on `stream`, waited for); calls before that compute the
- * activation directly, with identical results.
+ * are in elements.
  * Constraints: D in {64, 128}; inner % 8 == 0; I = D * popcount(input_mask) <= 384.
  */
 WGKV_API int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk_sh, int64_t pk_st,

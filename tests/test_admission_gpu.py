@@ -295,38 +295,3 @@ def test_gate_conv_path_matches_reference(wgkv, name):
     gp.g_fast_path = True
     assert (bits(gp(*x)) != got).sum() > got.size // 20
 
-
-def _gate_bits_wide(wgkv, act, fast, seed=4):
-    """Gate scores over inputs spread across many binades (hidden pre-activations from ~1e-6 to ~1e3)."""
-    torch.manual_seed(seed)
-    B, Hk, L, D, inner = 1, 4, 2048, 128, 64
-    gp = wgkv.GatingPredictor(D, Hk, ["pre_k"], act, inner / D, 1e-3, False, fast).cuda().bfloat16()
-    with torch.no_grad():
-        gp.conv1.weight.mul_(torch.logspace(-4, 2.5, Hk * inner, device="cuda").view(-1, 1, 1).bfloat16())
-    x = (torch.randn(B, Hk, L, D, device="cuda") * torch.logspace(-2, 1, L, device="cuda").view(1, 1, L, 1))
-    xb = x.bfloat16()
-    s = gp(xb, xb, xb)
-    torch.cuda.synchronize()
-    return bits(s)
-
-
-@pytest.mark.parametrize("act,fast", [("gelu", True), ("silu", False)])
-def test_activation_table_gives_the_computed_bits(wgkv, act, fast, tmp_path):
-    """The gate kernel's activation table (built on first use) returns exactly what computing the
-    activation does: scores with the table equal, bit for bit, those of a process that has it off."""
-    import os
-    import subprocess
-    import sys
-    got = _gate_bits_wide(wgkv, act, fast)
-    script = tmp_path / "gate_nolut.py"
-    script.write_text(
-        "import sys, numpy as np\n"
-        f"sys.path[:0] = {[os.path.dirname(os.path.abspath(__file__)), os.path.dirname(os.path.dirname(os.path.abspath(wgkv.__file__)))]!r}\n"
-        "import wgkv\n"
-        "from test_admission_gpu import _gate_bits_wide\n"
-        f"np.save(sys.argv[1], _gate_bits_wide(wgkv, {act!r}, {fast!r}))\n")
-    out = tmp_path / "ref.npy"
-    env = dict(os.environ, WGKV_GATE_LUT="0")
-    subprocess.run([sys.executable, str(script), str(out)], check=True, env=env, timeout=600)
-    ref = np.load(out)
-    assert np.array_equal(got, ref)

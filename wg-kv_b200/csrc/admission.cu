@@ -15,8 +15,6 @@
 // modeling_qwen3.py:236-239) and the device copy of the ring position that
 // lets a decode step replay as a CUDA graph.
 #include <math.h>
-
-#include <mutex>
 #include <string.h>
 
 #include "common.cuh"
@@ -60,7 +58,6 @@ struct GateParams {
   int B, Hk, L, D, I, inner, act;  // act: WGKV_GATE_SILU | WGKV_GATE_CONV bits
   const uint16_t *w1, *b1, *w2, *b2;
   float eps, thr, floor;             // floor: bf16 score floor of the conv path (-inf on the fast path)
-  int use_lut;                       // the activation table has been built on this device
   uint16_t* scores;
   int64_t ssb, ssh, sst;
   uint8_t* mask;
@@ -87,33 +84,6 @@ WGKV_DEV float gate_score(float dot, float bias, int act, float floor) {
   return s < floor ? floor : s;
 }
 
-// ---- activation table ----------------------------------------------------------------------
-// The activation's input is a bf16 value (the rounded hidden pre-activation) and its output is
-// rounded to bf16, so act is a function from bf16 to bf16: tabulated once per device for every
-// input with |h| in [2^-8, 2^8) (sign, 16 binades, 7 mantissa bits: 4096 entries per activation) by
-// the same act_fn the kernels use, so a looked-up value equals the computed one bit for bit.
-// Inputs outside that range (rare: tiny, huge, zero, non-finite) are computed directly.
-constexpr int kActLutBinLo = 127 - 8;  // float exponent field of 2^-8
-constexpr int kActLut = 4096;
-__device__ uint16_t g_act_lut[2][kActLut];
-
-__global__ void act_lut_init_kernel() {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= 2 * kActLut) return;
-  const int a = i / kActLut, e = i % kActLut;
-  const uint32_t bits = (uint32_t(e >> 11) << 31) | (uint32_t(kActLutBinLo + ((e >> 7) & 15)) << 23) |
-                        (uint32_t(e & 127) << 16);
-  g_act_lut[a][e] = f2bf(bf16_round(act_fn(__uint_as_float(bits), a ? WGKV_GATE_SILU : 0)));
-}
-
-// bf16(act(h)) for a bf16-valued h: from the shared-memory copy of the table when h is in range
-WGKV_DEV float act_lookup(float h, const uint16_t* lut, int act) {
-  const uint32_t u = __float_as_uint(h);
-  const uint32_t e = ((u >> 23) & 0xffu) - uint32_t(kActLutBinLo);  // wraps below the range
-  if (e < 16u) return bf2f(lut[((u >> 31) << 11) | (e << 7) | ((u >> 16) & 127u)]);
-  return bf16_round(act_fn(h, act));
-}
-
 __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int I = p.I, RS = I + 8;  // padded row stride (elements): conflict-free ldmatrix
@@ -121,7 +91,6 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
   uint16_t* ws = xs + kGateRows * RS;
   float* b1s = reinterpret_cast<float*>(ws + kGateChunk * RS);
   float* w2s = b1s + kGateChunk;
-  uint16_t* lut = reinterpret_cast<uint16_t*>(w2s + kGateChunk);  // this activation's table, or none
   const int h = blockIdx.y;
   const int row0 = blockIdx.x * kGateRows;
   const int nrows = p.B * p.L;
@@ -178,10 +147,6 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
     }
   }
 
-  if (p.use_lut) {
-    const uint4* src = reinterpret_cast<const uint4*>(g_act_lut[(p.act & WGKV_GATE_SILU) ? 1 : 0]);
-    for (int e = tid; e < kActLut / 8; e += kGateThreads) reinterpret_cast<uint4*>(lut)[e] = src[e];
-  }
   const int g = lane >> 2, t4 = lane & 3, mi = lane >> 3, ri = lane & 7;
   float part0 = 0.f, part1 = 0.f;
   const uint16_t* w1h = p.w1 + int64_t(h) * p.inner * I;
@@ -226,13 +191,8 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateParams p) {
         const float bb = b1s[n], ww = w2s[n];
         float h0 = gate_hidden(acc[j][e], bb, p.act);
         float h1 = gate_hidden(acc[j][2 + e], bb, p.act);
-        if (p.use_lut) {
-          part0 += act_lookup(h0, lut, p.act) * ww;
-          part1 += act_lookup(h1, lut, p.act) * ww;
-        } else {
-          part0 += bf16_round(act_fn(h0, p.act)) * ww;
-          part1 += bf16_round(act_fn(h1, p.act)) * ww;
-        }
+        part0 += bf16_round(act_fn(h0, p.act)) * ww;
+        part1 += bf16_round(act_fn(h1, p.act)) * ww;
       }
     }
   }
@@ -813,27 +773,6 @@ bool ring_pos_ok(const wgkv_pool* P, int pos) {
 
 using namespace wgkv;
 
-// Builds the activation table on `dev` the first time a gate call runs there outside stream
-// capture (one small launch on the caller's stream, then a wait for it); calls made while the
-// table is not built compute the activation directly.  Either way the results are the same bits.
-static bool act_lut_ready(int dev, cudaStream_t stream) {
-  static std::mutex mu;
-  static bool ready[64] = {false};
-  static const bool disabled = [] {  // WGKV_GATE_LUT=0: always compute the activation directly
-    const char* e = getenv("WGKV_GATE_LUT");
-    return e && e[0] == '0';
-  }();
-  if (disabled || dev < 0 || dev >= 64) return false;
-  std::lock_guard<std::mutex> lk(mu);
-  if (ready[dev]) return true;
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
-  act_lut_init_kernel<<<(2 * kActLut + 255) / 256, 256, 0, stream>>>();
-  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess) return false;
-  ready[dev] = true;
-  return true;
-}
-
 // The conv path's clamp floor as torch applies it to a bf16 tensor: g_epsilon rounded to bf16
 // (round to nearest even); the fast path has no floor.
 static float gate_floor(int act, float score_floor) {
@@ -898,11 +837,10 @@ extern "C" int wgkv_gate_scores(const uint16_t* pre_k, int64_t pk_sb, int64_t pk
   p.msh = m_sh;
   p.mst = m_st;
   const int RS = p.I + 8;
-  const size_t smem = size_t(kGateRows + kGateChunk) * RS * 2 + 2 * kGateChunk * 4 + kActLut * 2;
+  const size_t smem = size_t(kGateRows + kGateChunk) * RS * 2 + 2 * kGateChunk * 4;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  p.use_lut = act_lut_ready(dev, as_stream(stream)) ? 1 : 0;
   if (dev < 64 && !attr[dev]) {
     if (cudaFuncSetAttribute(gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
       return WGKV_ECUDA;
