@@ -479,7 +479,8 @@ def gpu_arm(args, rank, world, local_rank, emit=True, steps=None, extras=True):
         # C5: KV heads sharded over the N GPUs of this run, o_proj all-reduce per layer
         c5 = c5_arm(args, rank, world, local_rank, emit=False, steps=min(K, 16))
         c5 = {k: c5[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling",
-                                 "per_gpu_tok_s", "per_layer_us", "per_layer_us_note", "nccl_baseline", "e2e",
+                                 "per_gpu_tok_s", "fused_projection", "per_layer_us", "per_layer_us_note",
+                                 "nccl_baseline", "e2e",
                                  "attn_hbm_gbs_per_gpu", "attn_hbm_frac_per_gpu", "roofline", "gpu_launches")}
         c5["config"] = {"workload": "C5 decode: B=64, 256K ctx, KV heads 8/N per GPU, o_proj + sum over GPUs fused",
                         "parallelism": f"tp{world} (KV heads)", "note": "resident layer pools cycled when the "
@@ -760,7 +761,11 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     gw = torch.Generator(device=dev)
     gw.manual_seed(99)  # same full weights on every rank
     # o_proj + sum over GPUs as one kernel over NVLink peer memory (the NCCL path is timed beside it)
-    peers = PeerGroup(max_rows=B, max_cols=hidden, device=dev)
+    try:
+        peers = PeerGroup(max_rows=B, max_cols=hidden, device=dev)
+    except RuntimeError as e:  # raised on every rank alike: the step then uses GEMM + NCCL
+        print(f"rank {rank}: fused projection unavailable ({e}); using NCCL", file=sys.stderr)
+        peers = None
     tp_layers = []
     for l in range(Ly):
         w_full = (torch.randn(hidden, Hq_all * D, generator=gw, device=dev) * (Hq_all * D) ** -0.5).to(torch.bfloat16)
@@ -841,6 +846,7 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     for t in tp_layers:
         t.peers = peers
     wgkv.check_errors()
+    fused = peers is not None
 
     # end to end: each step's q/k/v/pre-k rows come from pinned host memory and the step's output
     # (the last layer's all-reduced o_proj rows) goes back, double-buffered on a copy stream
@@ -915,7 +921,8 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
     ach = kbytes / (kms / 1e3) / 1e9
     barrier()
     torch.cuda.synchronize()
-    peers.close()
+    if peers is not None:
+        peers.close()
     del cache, layers, tp_layers, inputs, qbuf, host_in, host_q, peers
     torch.cuda.empty_cache()
     line = {"metric": "decode tok/s @256K ragged cache, KV heads sharded (Llama-8B shape, B=64, 32 layers)",
@@ -929,6 +936,7 @@ def c5_arm(args, rank, world, local_rank, emit=True, steps=None):
                                 f"cache does not fit: {resident} resident layer pools cycled over 32 layers"),
                        "parallelism": f"tp{world} (KV heads)", **C5_CFG},
             "per_gpu_tok_s": B / (ms / 1e3) / world,
+            "fused_projection": fused,
             "per_layer_us": phase,
             "per_layer_us_note": ("median over 2 instrumented steps x 32 layers, max over ranks; the sum over "
                                   "GPUs includes waiting for the slowest rank"),

@@ -94,15 +94,24 @@ class PeerGroup:
         torch.cuda.synchronize(self.device)  # the zeroed buffer must be visible before a peer maps it
         infos = [None] * self.world
         dist.all_gather_object(infos, (h.raw, off.value, align(pb)), group=group)
-        for r, (hr, offr, flag_off) in enumerate(infos):
-            if r == self.rank:
-                self.struct.partial[r], self.struct.flags[r] = own
-                continue
-            peer_base = _ipc_open(hr) + offr
-            self._handles.append(hr)
-            self.struct.partial[r] = peer_base
-            self.struct.flags[r] = peer_base + flag_off
-        dist.barrier(group=group)
+        error = None
+        try:
+            for r, (hr, offr, flag_off) in enumerate(infos):
+                if r == self.rank:
+                    self.struct.partial[r], self.struct.flags[r] = own
+                    continue
+                peer_base = _ipc_open(hr) + offr
+                self._handles.append(hr)
+                self.struct.partial[r] = peer_base
+                self.struct.flags[r] = peer_base + flag_off
+        except RuntimeError as e:  # every rank still takes part in the agreement below
+            error = e
+        # all ranks agree on the outcome, so a failure on one rank raises on every rank
+        ok = torch.tensor([0 if error else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise RuntimeError(f"peer mapping failed on a rank of the group ({error or 'another rank'})")
 
     def close(self):
         """Unmap the peers' buffers (after the last call on every rank has completed)."""
