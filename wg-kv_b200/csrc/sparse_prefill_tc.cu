@@ -121,6 +121,19 @@ WGKV_DEV uint64_t exp2_fma2(uint64_t x) {
 #define WGKV_EMU_COUNT 1
 #endif
 
+// p = 2^x for one pair of scores, and its packed bf16 pair for P: by pair index on the FMA pipe
+// (exp2_fma2) or as two fp32 SFU ops.  (The packed bf16 SFU form, ex2.approx.ftz.bf16x2, for one,
+// two or all four pairs in four measured 3-5 % slower on the C3 shape.)
+WGKV_DEV void exp2_pair(int pi, uint64_t x2, float x0, float x1, float& p0, float& p1, uint32_t& packed) {
+  if ((pi % WGKV_EMU_PERIOD) < WGKV_EMU_COUNT) {
+    f2_split(exp2_fma2(x2), p0, p1);
+  } else {
+    p0 = fast_exp2(x0);
+    p1 = fast_exp2(x1);
+  }
+  packed = pack_bf16x2(p0, p1);
+}
+
 struct TcParams {
   int B, L, Hk, G, R, n_hg;
   const int32_t *bc, *bo, *cc, *ci;
@@ -445,22 +458,10 @@ __global__ void __launch_bounds__(Tc<D, NM, HV>::kThreads, 1)
           f2_split(xa, x0, x1);
           f2_split(xb, x2, x3);
           const int pi = (cc + c) >> 1;  // index of the pair (x0, x1); (x2, x3) is pi + 1
-          if ((pi % WGKV_EMU_PERIOD) < WGKV_EMU_COUNT) {
-            f2_split(exp2_fma2(xa), p0, p1);
-          } else {
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
-          }
-          if (((pi + 1) % WGKV_EMU_PERIOD) < WGKV_EMU_COUNT) {
-            f2_split(exp2_fma2(xb), p2, p3);
-          } else {
-            p2 = fast_exp2(x2);
-            p3 = fast_exp2(x3);
-          }
+          exp2_pair(pi, xa, x0, x1, p0, p1, pk[c >> 1]);
+          exp2_pair(pi + 1, xb, x2, x3, p2, p3, pk[(c >> 1) + 1]);
           sa = add2(sa, f2(p0, p1));
           sb = add2(sb, f2(p2, p3));
-          pk[c >> 1] = pack_bf16x2(p0, p1);
-          pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
         }
         tmem_st16(trow + ((hf * KPT + cc) >> 1), pk);
       }
