@@ -541,57 +541,69 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
     const int i = i0 + k;
     const int gl = P.global_lengths[i];
     int32_t* trow = P.block_table + int64_t(i) * P.max_blocks_per_head + W / T;
-    int pid;
-    if (gl % T == 0) {
+    if (gl % T == 0) {  // a new page for this token
       const int r = next++;
-      pid = r < s_nff ? P.free_ids[s_fc - s_nff + r] : s_nf + (r - s_nff);
-      trow[gl / T] = pid;
-    } else {
-      pid = trow[gl / T];
+      trow[gl / T] = r < s_nff ? P.free_ids[s_fc - s_nff + r] : s_nf + (r - s_nff);
     }
+    P.global_lengths[i] = gl + 1;
+  }
+  __syncthreads();  // tables and lengths written: the copies below read them back
+  // ---- row copies: 8 lanes per promoted (layer, b, h), every load of a row issued before its
+  // stores; the page's key bounds (:744-761) are updated from the same loads ----
+  const int grp = threadIdx.x >> 3, gl8 = threadIdx.x & 7;
+  const int nv = D / 8;  // 16-byte vectors per row (8 or 16)
+  for (int i = grp; i < N; i += kPromoteThreads / 8) {
+    if (!P.local_is_global[int64_t(i) * W + ptr]) continue;
+    const int gl = P.global_lengths[i] - 1;  // the length before this promotion
+    const int pid = P.block_table[int64_t(i) * P.max_blocks_per_head + W / T + gl / T];
     const int64_t dst = int64_t(pid) * T + gl % T;
     const int64_t src = int64_t(i) * W + ptr;
     const uint4* ks = reinterpret_cast<const uint4*>(P.k + src * D);
     const uint4* vs = reinterpret_cast<const uint4*>(P.v + src * D);
-    uint4* kd = reinterpret_cast<uint4*>(P.k + dst * D);
-    uint4* vd = reinterpret_cast<uint4*>(P.v + dst * D);
-    for (int c = 0; c < D / 8; ++c) {
-      kd[c] = ks[c];
-      vd[c] = vs[c];
+    uint4 kr[2], vr[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = gl8 + 8 * u;
+      if (c < nv) {
+        kr[u] = ks[c];
+        vr[u] = vs[c];
+      }
     }
-    if (P.quest_min) {  // page key bounds (:744-761): a new page starts at the key
-      uint4* mn = reinterpret_cast<uint4*>(P.quest_min + int64_t(pid) * D);
-      uint4* mx = reinterpret_cast<uint4*>(P.quest_max + int64_t(pid) * D);
-      const bool fresh = gl % T == 0;
-#pragma unroll 4
-      for (int c = 0; c < D / 8; ++c) {
-        const uint4 kv = ks[c];
-        if (fresh) {
-          mn[c] = kv;
-          mx[c] = kv;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = gl8 + 8 * u;
+      if (c >= nv) continue;
+      reinterpret_cast<uint4*>(P.k + dst * D)[c] = kr[u];
+      reinterpret_cast<uint4*>(P.v + dst * D)[c] = vr[u];
+      if (P.quest_min) {  // page key bounds: a new page starts at the key
+        uint4* mn = reinterpret_cast<uint4*>(P.quest_min + int64_t(pid) * D) + c;
+        uint4* mx = reinterpret_cast<uint4*>(P.quest_max + int64_t(pid) * D) + c;
+        const uint4 kv = kr[u];
+        if (gl % T == 0) {
+          *mn = kv;
+          *mx = kv;
         } else {
-          const uint4 a = mn[c], z = mx[c];
+          const uint4 a = *mn, z = *mx;
           const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, aw[4] = {a.x, a.y, a.z, a.w}, zw[4] = {z.x, z.y, z.z, z.w};
           uint32_t lo[4], hi[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {  // two bf16 per word: keep each half's min / max bits
-            uint32_t l = 0, u = 0;
+            uint32_t l = 0, h2 = 0;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
               const uint32_t sh = 16 * half;
               const uint16_t kb = uint16_t(kw[e] >> sh), ab = uint16_t(aw[e] >> sh), zb = uint16_t(zw[e] >> sh);
               l |= uint32_t(bf2f(kb) < bf2f(ab) ? kb : ab) << sh;
-              u |= uint32_t(bf2f(kb) > bf2f(zb) ? kb : zb) << sh;
+              h2 |= uint32_t(bf2f(kb) > bf2f(zb) ? kb : zb) << sh;
             }
             lo[e] = l;
-            hi[e] = u;
+            hi[e] = h2;
           }
-          mn[c] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-          mx[c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *mn = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *mx = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         }
       }
     }
-    P.global_lengths[i] = gl + 1;
   }
 }
 
