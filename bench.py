@@ -455,7 +455,7 @@ def gpu_arm(args, rank, world, local_rank, emit=True, steps=None, extras=True):
     h2d_step = int((inputs[0].numel() + qbuf[0].numel()) * 2)  # the bytes the e2e loop uploads per step
     d2h_step = int(outbuf.numel() * 2)
     prefill = c4 = c5 = None
-    extras = extras and args.workload == "decode" and not args.small
+    extras = extras and args.workload == "decode" and not args.small and not args.no_extras
     if extras:
         # release the decode state (the pool views of the roofline timing included) before the next workload
         del cache, layers, inputs, qbuf, outbuf, outs, host_in, host_q, dev_in, dev_q, host_out
@@ -1209,6 +1209,7 @@ def main():
     ap.add_argument("--no-defer", action="store_true", help="model workload: gate each token at decode")
     ap.add_argument("--small", action="store_true", help="reduced layer count for profiling captures")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 400K prefill measurement of the default run")
+    ap.add_argument("--no-extras", action="store_true", help="the default run without its C3/C4/C5 sub-records")
     args = ap.parse_args()
     global METRIC, WORKLOAD_NAME
     if args.workload == "qwen3_decode":

@@ -179,7 +179,8 @@ WGKV_API int wgkv_prefill_admit(const wgkv_pool* pool, int layer, int seq_len, c
  * head's global pages (a new page from next_free_block when the length is a multiple of `page`,
  * allocated in (layer, b, h) order) and bump global_lengths.  One launch for all layers, as the
  * reference does at layer 0 when the ring is full (:1470-1471).  Capacity violations write nothing
- * and set err.  local_ptr = WGKV_RING_ON_DEVICE: the slot is ring_state[1], and nothing happens while
+ * and set err; while err holds a capacity error (not yet cleared by the caller) promotions do nothing.
+ * Two launches: the allocation pass (one CTA) and the row copies (one CTA per 32 heads).  local_ptr = WGKV_RING_ON_DEVICE: the slot is ring_state[1], and nothing happens while
  * ring_state[0] < window (the reference promotes only once the ring is full, :1470).
  */
 WGKV_API int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream);

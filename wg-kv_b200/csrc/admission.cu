@@ -474,11 +474,14 @@ constexpr int kPromoteMaxPer = 32;  // (layer, b, h) entries per thread: up to 3
 __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, int ptr) {
   const wgkv_pool& P = pa.P;
   const int N = P.layers * P.batch * P.kv_heads;
-  const int W = P.window, T = P.page, D = P.head_dim;
+  const int W = P.window, T = P.page;
   if (ptr < 0) {  // position on the device: promote only once the ring is full (:1470)
     if (P.ring_state[0] < W) return;
     ptr = P.ring_state[1];
   }
+  // a capacity error already flagged (and not yet read by the host) stops promotions: the
+  // reference has aborted at that point, and the copy kernel relies on it
+  if (P.err && (*P.err & (WGKV_ERR_HEAD_CAPACITY | WGKV_ERR_POOL_EXHAUSTED))) return;
   const int per = (N + kPromoteThreads - 1) / kPromoteThreads;
   const int i0 = threadIdx.x * per;  // contiguous entries keep the (layer, b, h) allocation order
   __shared__ int wsum[kPromoteThreads / 32];
@@ -547,13 +550,26 @@ __global__ void __launch_bounds__(kPromoteThreads) promote_kernel(PoolArgs pa, i
     }
     P.global_lengths[i] = gl + 1;
   }
-  __syncthreads();  // tables and lengths written: the copies below read them back
-  // ---- row copies: 8 lanes per promoted (layer, b, h), every load of a row issued before its
-  // stores; the page's key bounds (:744-761) are updated from the same loads ----
-  const int grp = threadIdx.x >> 3, gl8 = threadIdx.x & 7;
+}
+
+// The row copies of a promotion, after promote_kernel wrote the tables and lengths: 8 lanes per
+// promoted (layer, b, h), 32 of them per CTA, every load of a row issued before its stores; the
+// page's key bounds (:744-761) are updated from the same loads.  Nothing is copied when the pool's
+// error word holds a capacity error (promote_kernel then changed nothing either).
+__global__ void __launch_bounds__(256) promote_copy_kernel(PoolArgs pa, int ptr) {
+  const wgkv_pool& P = pa.P;
+  const int N = P.layers * P.batch * P.kv_heads;
+  const int W = P.window, T = P.page, D = P.head_dim;
+  if (ptr < 0) {
+    if (P.ring_state[0] < W) return;
+    ptr = P.ring_state[1];
+  }
+  if (P.err && (*P.err & (WGKV_ERR_HEAD_CAPACITY | WGKV_ERR_POOL_EXHAUSTED))) return;
+  const int gl8 = threadIdx.x & 7;
   const int nv = D / 8;  // 16-byte vectors per row (8 or 16)
-  for (int i = grp; i < N; i += kPromoteThreads / 8) {
-    if (!P.local_is_global[int64_t(i) * W + ptr]) continue;
+  const int i = blockIdx.x * 32 + (threadIdx.x >> 3);
+  if (i >= N || !P.local_is_global[int64_t(i) * W + ptr]) return;
+  {
     const int gl = P.global_lengths[i] - 1;  // the length before this promotion
     const int pid = P.block_table[int64_t(i) * P.max_blocks_per_head + W / T + gl / T];
     const int64_t dst = int64_t(pid) * T + gl % T;
@@ -923,6 +939,9 @@ extern "C" int wgkv_promote(const wgkv_pool* pool, int local_ptr, void* stream) 
   PoolArgs pa{*pool};
   if (pool->layers * pool->batch * pool->kv_heads > kPromoteThreads * kPromoteMaxPer) return WGKV_EINVAL;
   promote_kernel<<<1, kPromoteThreads, 0, as_stream(stream)>>>(pa, local_ptr);
+  if (cudaGetLastError() != cudaSuccess) return WGKV_ECUDA;
+  const int N = pool->layers * pool->batch * pool->kv_heads;
+  promote_copy_kernel<<<(N + 31) / 32, 256, 0, as_stream(stream)>>>(pa, local_ptr);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 

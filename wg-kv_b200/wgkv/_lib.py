@@ -88,7 +88,7 @@ class _Lib:
 
 
 # kernels each compute entry point launches (for the benchmark's launch count)
-KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_append": 1, "wgkv_decode_gate_append": 1, "wgkv_promote": 1,
+KERNELS_PER_CALL = {"wgkv_paged_decode": 1, "wgkv_gate_scores": 1, "wgkv_decode_append": 1, "wgkv_decode_gate_append": 1, "wgkv_promote": 2,
                     "wgkv_prefill_admit": 3, "wgkv_sparse_indices": 3, "wgkv_sparse_prefill": 1, "wgkv_sparse_prefill_pooled": 1, "wgkv_gather_columns": 1,
                     "wgkv_paged_decode_noalloc": 1, "wgkv_ring_advance": 1, "wgkv_decode_prologue": 1,
                     "wgkv_rms_norm": 1, "wgkv_silu_mul": 1, "wgkv_skinny_gemm": 1, "wgkv_quest_select": 2, "wgkv_argmax": 1,
