@@ -1060,7 +1060,9 @@ def quest_arm(args, rank, world, local_rank):
                 "window": win, "evict_ratio": ratio, "kernel_size": ks, "tokens_before": before,
                 "tokens_after": after, "pages_freed": int(free_n.item()),
                 "score_tflops": flops / (evict_ms / 1e3) / 1e12,
-                "kernels": "snap_rowstats / snap_scores (mma.sync) + snap_select_compact + snap_free"}
+                "kernels": ("snap_rowstats / snap_scores (mma.sync)" if os.environ.get("WGKV_SNAPKV_MMA_SYNC") == "1"
+                            else "snap_rowstats_tc / snap_scores_tc (tcgen05)")
+                + " + snap_select_compact + snap_free"}
     peak, kind = peaks()
     if rank == 0:
         line = {

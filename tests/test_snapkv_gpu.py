@@ -80,7 +80,11 @@ def test_snapkv_golden_pipeline():
 
 
 @pytest.mark.parametrize("B,Hk,G,D,win,ks,ratio", [(2, 2, 4, 128, 32, 5, 0.3), (1, 4, 2, 64, 64, 3, 0.55),
-                                                   (1, 2, 8, 128, 16, 7, 1.0)])
+                                                   (1, 2, 8, 128, 16, 7, 1.0),
+                                                   # several 256-row chunks / a 16-row last chunk / a
+                                                   # half-filled 32-row piece / G = 16 (tensor-core passes)
+                                                   (1, 2, 4, 128, 256, 5, 0.3), (1, 1, 4, 128, 260, 5, 0.3),
+                                                   (2, 2, 2, 64, 40, 3, 0.4), (1, 1, 16, 128, 16, 5, 0.3)])
 def test_snapkv_evict_matches_oracle(B, Hk, G, D, win, ks, ratio):
     import wgkv
     W, T, L = 64, 16, 2500

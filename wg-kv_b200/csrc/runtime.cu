@@ -36,6 +36,21 @@ bool encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS;
 }
 
+bool encode_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t stride_elems[2],
+                    const uint32_t box[3], bool swizzle128) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return false;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {stride_elems[0] * 2, stride_elems[1] * 2};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, st, bx, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int device_sms() {
   static int cache[64] = {0};
   int dev = 0;

@@ -11,9 +11,10 @@
 // Numerics follow the reference's torch expressions: the q . k products accumulate in fp32 and are
 // rounded to bf16, the scaled score is rounded to bf16 again, the softmax is fp32.
 //
-// Kernels (per layer): row statistics (online max / sum over all keys, one CTA per 128 window
-// rows); key scores (one CTA per 64-key chunk, all window rows, mma.sync m16n8k16); select +
-// compact (one CTA per head).  After all layers: free-list append (one CTA).
+// Kernels (per layer): row statistics and key scores on the tensor cores (snapkv_tc.cu) where the
+// shape fits them, else here on mma.sync m16n8k16 (row statistics: online max / sum over all
+// keys, one CTA per 128 window rows; key scores: one CTA per 64-key chunk, all window rows);
+// select + compact (one CTA per head).  After all layers: free-list append (one CTA).
 #include "common.cuh"
 
 namespace wgkv {
@@ -379,6 +380,11 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
 }  // namespace wgkv
 
+namespace wgkv {
+int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int win, int Hq, float scale,
+                     float2* rowml, float* scores, cudaStream_t s);  // snapkv_tc.cu
+}
+
 using namespace wgkv;
 
 extern "C" size_t wgkv_snapkv_workspace_size(const wgkv_pool* pool, int window, int q_heads) {
@@ -441,13 +447,20 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
     a.layer = l;
     sa.layer = l;
     const dim3 g1((a.R + kRowsPerCta - 1) / kRowsPerCta, BH), g2(max_chunks, BH);
+    // the two score passes on the tensor cores where the shape fits them, else on mma.sync
+    const int tc = snapkv_scores_tc(*pool, l, queries, window, q_heads, softmax_scale, a.rowml, a.scores, s);
+    if (tc != 1 && tc != WGKV_OK) return tc;
     if (D == 128) {
-      snap_rowstats_kernel<128><<<g1, kSnThreads, smem_keys, s>>>(a);
-      snap_scores_kernel<128><<<g2, kSnThreads, smem_scores, s>>>(a);
+      if (tc == 1) {
+        snap_rowstats_kernel<128><<<g1, kSnThreads, smem_keys, s>>>(a);
+        snap_scores_kernel<128><<<g2, kSnThreads, smem_scores, s>>>(a);
+      }
       snap_select_compact_kernel<128><<<BH, kSnThreads, smem_stage, s>>>(sa);
     } else {
-      snap_rowstats_kernel<64><<<g1, kSnThreads, smem_keys, s>>>(a);
-      snap_scores_kernel<64><<<g2, kSnThreads, smem_scores, s>>>(a);
+      if (tc == 1) {
+        snap_rowstats_kernel<64><<<g1, kSnThreads, smem_keys, s>>>(a);
+        snap_scores_kernel<64><<<g2, kSnThreads, smem_scores, s>>>(a);
+      }
       snap_select_compact_kernel<64><<<BH, kSnThreads, smem_stage, s>>>(sa);
     }
   }

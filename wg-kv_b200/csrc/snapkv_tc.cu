@@ -1,0 +1,489 @@
+// SnapKV key scoring on the 5th-gen tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// The two contraction passes of the eviction in snapkv.cu (reference snapkv_evict,
+// src/modeling_layers.py:616-626: softmax of the window queries against a head's global keys, max
+// over the query group, mean over the window), with the same numerics as the mma.sync kernels
+// there: q . k accumulated in fp32 and rounded to bf16, times the scale rounded to bf16 again,
+// then an fp32 softmax (expf, online max / sum in 128-key steps).
+//
+//   pass 1  row statistics.  One CTA per (head, 256 window rows): two M-tiles of 128 rows (Q
+//           resident in shared memory), K tiles of 128 keys streamed by TMA (one box per page
+//           and 64 columns) through a 3-stage ring; S = Q K^T (M=128, N=128) into a double-
+//           buffered TMEM slot per M-tile; one warpgroup per M-tile, a thread per row (TMEM lane
+//           = row), keeps the running max and sum of exp.
+//   pass 2  key scores, transposed: the keys are the M dimension, so a thread owns a key and
+//           sees all window rows of its TMEM lane, and the max over the group and the sum over
+//           the window need no exchange between threads.  One CTA per (head, every gridDim.x-th
+//           128-key tile): S^T = K Q^T (M=128 keys, N=256 window rows per MMA, Q chunks streamed
+//           by TMA through a 2-stage ring); the CTA's tiles go in pairs, one per warpgroup, each
+//           with its own 256-column TMEM slot, and both tiles of a pair share every Q chunk.
+//
+// Warp 0 issues the TMA loads (no multicast), lane 0 of warp 1 the MMAs; every wait is bounded and
+// a wait that runs out sets WGKV_ERR_TIMEOUT in the pool's error word (outputs are then undefined).
+#include "common.cuh"
+#include "runtime.h"
+#include "tc.cuh"
+
+namespace wgkv {
+namespace {
+
+constexpr int kTK = 128;       // keys per K tile
+constexpr int kNC = 256;       // window rows per pass-2 MMA
+constexpr int kMaxRows = 2048; // window rows per head (win x G) the pass-2 statistics table holds
+
+template <int D>
+struct SnL {
+  static constexpr int kDB = D / 64;          // 64-column boxes per row
+  static constexpr int kBox = 128 * 128;      // one box of 128 rows x 128 B
+  static constexpr int kKTile = kDB * kBox;   // 128 keys
+  static constexpr int kQ1 = kDB * kBox;      // pass 1: one 128-row M-tile of Q
+  static constexpr int kQ2 = kDB * 2 * kBox;  // pass 2: one 256-row chunk of Q
+  static constexpr int kK1 = 3;               // pass-1 K stages
+  static constexpr int kSmem1 = 2 * kQ1 + kK1 * kKTile + 256 + 1024;
+  static constexpr int kSmem2 = 2 * kKTile + 2 * kQ2 + kMaxRows * 8 + 256 + 1024;
+};
+
+constexpr int kSnTcThreads = 384;  // warpgroup 0: TMA, MMA, two idle warps; two compute warpgroups
+
+struct SnTcArgs {
+  int layer, B, Hk, G, win, R, T, window_pages, max_blocks, max_tok;
+  const int32_t* block_table;
+  const int32_t* lengths;
+  float scale, inv_win;
+  float2* rowml;   // [BH][R] (max, sum)
+  float* scores;   // [BH][max_tok]
+  int* err;
+};
+
+WGKV_DEV uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+WGKV_DEV void f2_split(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+WGKV_DEV uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// (x0, x1) <- bf16(bf16(x) * scale), the rounding of torch.matmul(bf16) * scaling on bf16 tensors
+WGKV_DEV void round_scaled2(float& x0, float& x1, uint64_t sc2) {
+  uint32_t p = pack_bf16x2(x0, x1);
+  float y0, y1;
+  f2_split(mul2(f2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u)), sc2), y0, y1);
+  p = pack_bf16x2(y0, y1);
+  x0 = __uint_as_float(p << 16);
+  x1 = __uint_as_float(p & 0xFFFF0000u);
+}
+
+// K tile `kt` of a head (pages of T rows, T | 128) into `dst`: lane i issues page i's boxes.
+// Pages past the head's last one repeat it (their keys are masked or never stored).
+template <int D>
+WGKV_DEV void load_k_tile(int lane, uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, const int32_t* grow, int nb,
+                          int kt, int T) {
+  const int ppt = kTK / T;
+  for (int pi = lane; pi < ppt; pi += 32) {
+    const int pg = min(kt * ppt + pi, nb - 1);
+    const int id = __ldg(grow + pg);
+#pragma unroll
+    for (int d = 0; d < SnL<D>::kDB; ++d) tma_load_2d(dst + d * SnL<D>::kBox + pi * T * 128, tm, bar, d * 64, id * T);
+  }
+}
+
+// ============================== pass 1: row statistics ==============================
+struct Bars1 {
+  uint64_t qfull;
+  uint64_t kfull[SnL<128>::kK1], kempty[SnL<128>::kK1];
+  uint64_t sfull[2][2], sfree[2][2];
+  uint32_t tmem;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kSnTcThreads, 1)
+    snap_rowstats_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            SnTcArgs a) {
+  using L = SnL<D>;
+  constexpr int kStg = L::kK1;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm + 2 * L::kQ1;
+  Bars1* bar = reinterpret_cast<Bars1*>(sK + kStg * L::kKTile);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / a.Hk, h = bh - b * a.Hk;
+  const int glen = a.lengths[int64_t(a.layer) * a.B * a.Hk + bh];
+  if (glen <= 0) return;
+  const int row0 = blockIdx.x * 256;
+  const int nt = min(2, (a.R - row0 + 127) / 128);  // M-tiles of this CTA
+  const int n = (glen + kTK - 1) / kTK;
+  const int nb = (glen + a.T - 1) / a.T;
+  const int32_t* grow = a.block_table + (int64_t(a.layer) * a.B * a.Hk + bh) * a.max_blocks + a.window_pages;
+
+  if (tid == 0) {
+    mbar_init(&bar->qfull, 1);
+    for (int s = 0; s < kStg; ++s) {
+      mbar_init(&bar->kfull[s], 1);
+      mbar_init(&bar->kempty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t)
+      for (int u = 0; u < 2; ++u) {
+        mbar_init(&bar->sfull[t][u], 1);
+        mbar_init(&bar->sfree[t][u], 4);
+      }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<512>(&bar->tmem);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;
+  bool ok = true;
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmK);
+      mbar_arrive_expect_tx(&bar->qfull, nt * L::kQ1);
+      const int z0 = (a.layer * a.B + b) * a.win;
+      for (int t = 0; t < nt; ++t)
+        for (int d = 0; d < L::kDB; ++d)
+          tma_load_3d(sm + t * L::kQ1 + d * L::kBox, &tmQ, &bar->qfull, d * 64, h * a.G, z0 + (row0 + t * 128) / a.G);
+    }
+    for (int j = 0; j < n; ++j) {
+      const int s = j % kStg;
+      if (!mbar_wait(&bar->kempty[s], ((j / kStg) & 1) ^ 1)) { ok = false; break; }
+      if (lane == 0) mbar_arrive_expect_tx(&bar->kfull[s], L::kKTile);
+      __syncwarp();
+      load_k_tile<D>(lane, sK + s * L::kKTile, &tmK, &bar->kfull[s], grow, nb, j, a.T);
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(128, kTK, 0, 0);
+      if (!mbar_wait(&bar->qfull, 0)) ok = false;
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j % kStg, u = j & 1;
+        if (!mbar_wait(&bar->kfull[s], (j / kStg) & 1)) { ok = false; break; }
+        const uint32_t ks = smem_u32(sK + s * L::kKTile);
+        for (int t = 0; t < nt; ++t) {
+          if (!mbar_wait(&bar->sfree[t][u], ((j >> 1) & 1) ^ 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qt = smem_u32(sm + t * L::kQ1);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t da = umma_desc_sw128(qt + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
+            const uint64_t db = umma_desc_sw128(ks + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
+            umma_ss(tmem + t * 256 + u * 128, da, db, idesc, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&bar->sfull[t][u]);
+        }
+        if (!ok) break;
+        umma_commit(&bar->kempty[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4 && (warp - 4) / 4 < nt) {
+    // ---------------- row statistics: a thread per window row ----------------
+    const int t = (warp - 4) / 4, quad = warp & 3;
+    const int r = row0 + t * 128 + quad * 32 + lane;
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
+    const uint64_t sc2 = f2(a.scale, a.scale);
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int u = j & 1;
+      if (!mbar_wait(&bar->sfull[t][u], (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      float sv[kTK];
+#pragma unroll
+      for (int c = 0; c < kTK; c += 32) tmem_ld32(trow + u * 128 + c, sv + c);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->sfree[t][u]);  // S is in registers: the slot may be refilled
+#pragma unroll
+      for (int c = 0; c < kTK; c += 2) round_scaled2(sv[c], sv[c + 1], sc2);
+      const int lim = glen - j * kTK;  // valid keys of this tile
+      if (lim < kTK) {
+#pragma unroll
+        for (int c = 0; c < kTK; ++c) sv[c] = c < lim ? sv[c] : -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int u8 = 0; u8 < 8; ++u8) mx[u8] = sv[u8];
+#pragma unroll
+      for (int c = 8; c < kTK; c += 8)
+#pragma unroll
+        for (int u8 = 0; u8 < 8; ++u8) mx[u8] = fmaxf(mx[u8], sv[c + u8]);
+      float x = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float nm = fmaxf(m, x);
+      float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kTK; c += 4)
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) e[u4] += expf(sv[c + u4] - nm);
+      l = l * expf(m - nm) + ((e[0] + e[1]) + (e[2] + e[3]));  // expf(-inf) = 0 on the first tile
+      m = nm;
+    }
+    if (ok && r < a.R) a.rowml[int64_t(bh) * a.R + r] = make_float2(m, l);
+  }
+  if (!ok) set_error(a.err, WGKV_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+// ============================== pass 2: key scores ==============================
+struct Bars2 {
+  uint64_t kfull[2], kempty[2], qfull[2], qempty[2];
+  uint64_t sfull[2], sfree[2];
+  uint32_t tmem;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kSnTcThreads, 1)
+    snap_scores_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          SnTcArgs a) {
+  using L = SnL<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm;
+  uint8_t* sQ = sm + 2 * L::kKTile;
+  float2* st = reinterpret_cast<float2*>(sQ + 2 * L::kQ2);  // per window row: (max, 1 / sum)
+  Bars2* bar = reinterpret_cast<Bars2*>(reinterpret_cast<uint8_t*>(st) + kMaxRows * 8);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / a.Hk, h = bh - b * a.Hk;
+  const int glen = a.lengths[int64_t(a.layer) * a.B * a.Hk + bh];
+  const int ntile = (glen + kTK - 1) / kTK;
+  if (int(blockIdx.x) >= ntile) return;
+  const int ni = (ntile - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);  // tiles of this CTA
+  const int nc = (a.R + kNC - 1) / kNC;                                             // Q chunks per tile
+  const int nb = (glen + a.T - 1) / a.T;
+  const int32_t* grow = a.block_table + (int64_t(a.layer) * a.B * a.Hk + bh) * a.max_blocks + a.window_pages;
+
+  for (int r = tid; r < a.R; r += kSnTcThreads) {
+    const float2 ml = a.rowml[int64_t(bh) * a.R + r];
+    st[r] = make_float2(ml.x, 1.f / ml.y);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->kfull[s], 1);
+      mbar_init(&bar->kempty[s], 1);
+      mbar_init(&bar->qfull[s], 1);
+      mbar_init(&bar->qempty[s], 1);
+      mbar_init(&bar->sfull[s], 1);
+      mbar_init(&bar->sfree[s], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<512>(&bar->tmem);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;
+  bool ok = true;
+  if (warp == 0) {
+    // ------- TMA producer: tiles in pairs (one per warpgroup); the pair's K, then Q chunks -------
+    if (lane == 0) {
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmK);
+    }
+    const int z0 = (a.layer * a.B + b) * a.win;
+    int q = 0;
+    for (int pr = 0; 2 * pr < ni && ok; ++pr) {
+      for (int w = 0; w < 2 && 2 * pr + w < ni; ++w) {
+        const int kt = blockIdx.x + (2 * pr + w) * gridDim.x;
+        if (!mbar_wait(&bar->kempty[w], (pr & 1) ^ 1)) { ok = false; break; }
+        if (lane == 0) mbar_arrive_expect_tx(&bar->kfull[w], L::kKTile);
+        __syncwarp();
+        load_k_tile<D>(lane, sK + w * L::kKTile, &tmK, &bar->kfull[w], grow, nb, kt, a.T);
+        __syncwarp();
+      }
+      for (int c = 0; c < nc && ok; ++c, ++q) {
+        const int qs = q & 1;
+        if (!mbar_wait(&bar->qempty[qs], ((q >> 1) & 1) ^ 1)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar->qfull[qs], L::kQ2);
+          for (int d = 0; d < L::kDB; ++d)
+            tma_load_3d(sQ + qs * L::kQ2 + d * 2 * L::kBox, &tmQ, &bar->qfull[qs], d * 64, h * a.G,
+                        z0 + c * (kNC / a.G));
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: S^T = K Q^T per (tile, chunk), a pair's tiles alternating ----------------
+    if (lane == 0) {
+      int q = 0;
+      for (int pr = 0; 2 * pr < ni && ok; ++pr) {
+        const int nw = min(2, ni - 2 * pr);  // tiles in this pair
+        for (int w = 0; w < nw; ++w)
+          if (!mbar_wait(&bar->kfull[w], pr & 1)) { ok = false; break; }
+        for (int c = 0; c < nc && ok; ++c, ++q) {
+          const int qs = q & 1, uw = pr * nc + c;  // uw-th use of each warpgroup's slot
+          if (!mbar_wait(&bar->qfull[qs], (q >> 1) & 1)) { ok = false; break; }
+          const int N = min(kNC, a.R - c * kNC);
+          const uint32_t idesc = umma_idesc_bf16(128, N, 0, 0);
+          const uint32_t qa = smem_u32(sQ + qs * L::kQ2);
+          for (int w = 0; w < nw; ++w) {
+            if (!mbar_wait(&bar->sfree[w], (uw & 1) ^ 1)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t ks = smem_u32(sK + w * L::kKTile);
+#pragma unroll
+            for (int k = 0; k < D / 16; ++k) {
+              const uint64_t da = umma_desc_sw128(ks + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
+              const uint64_t db = umma_desc_sw128(qa + (k >> 2) * 2 * L::kBox + (k & 3) * 32, 16, 1024);
+              umma_ss(tmem + w * 256, da, db, idesc, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&bar->sfull[w]);
+          }
+          if (!ok) break;
+          umma_commit(&bar->qempty[qs]);
+        }
+        if (!ok) break;
+        for (int w = 0; w < nw; ++w) umma_commit(&bar->kempty[w]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------- scores: a thread per key, warpgroup w takes tile w of every pair ----------------
+    const int w = (warp - 4) / 4, quad = warp & 3;
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + w * 256;
+    const uint64_t sc2 = f2(a.scale, a.scale);
+    const int G = a.G;
+    for (int i = w; i < ni && ok; i += 2) {
+      const int kt = blockIdx.x + i * gridDim.x;
+      float acc = 0.f;
+      for (int c = 0; c < nc; ++c) {
+        const int uw = (i >> 1) * nc + c;
+        if (!mbar_wait(&bar->sfull[w], uw & 1)) { ok = false; break; }
+        tc_fence_after();
+        const int ncols = min(kNC, a.R - c * kNC);
+        for (int p0 = 0; p0 < ncols; p0 += 32) {
+          float sv[32];
+          tmem_ld32(trow + p0, sv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int cc = 0; cc < 32; cc += 2) round_scaled2(sv[cc], sv[cc + 1], sc2);
+          const int rb = c * kNC + p0;  // window row of sv[0]
+          // rows rb + g*G .. rb + g*G + G - 1 (G a power of two dividing 32) are the G query heads
+          // of one window position: max over them, then the sum over window positions
+          float gm = 0.f;
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) {
+            const float2 ml = st[rb + cc];
+            float pr = expf(sv[cc] - ml.x) * ml.y;
+            pr = rb + cc < a.R ? pr : 0.f;
+            gm = (cc & (G - 1)) == 0 ? pr : fmaxf(gm, pr);
+            if ((cc & (G - 1)) == G - 1) acc += gm;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->sfree[w]);
+      }
+      const int key = kt * kTK + quad * 32 + lane;
+      if (ok && key < glen) a.scores[int64_t(bh) * a.max_tok + key] = acc * a.inv_win;
+    }
+  }
+  if (!ok) set_error(a.err, WGKV_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+}  // namespace
+
+// Per layer: the two score passes on the tensor cores.  Returns 1 when the shape does not fit
+// them (the caller runs the mma.sync kernels), else a WGKV status.
+int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int win, int Hq, float scale,
+                     float2* rowml, float* scores, cudaStream_t s) {
+  const int Hk = P.kv_heads, G = Hq / Hk, D = P.head_dim, T = P.page, R = win * G;
+  if (D != 64 && D != 128) return 1;
+  if (32 % G || R % 16 || R > kMaxRows || T % 8 || kTK % T) return 1;
+  if ((reinterpret_cast<uintptr_t>(queries) | reinterpret_cast<uintptr_t>(P.k)) & 15) return 1;
+  if (uint64_t(P.total_blocks) * T >= (uint64_t(1) << 31) ||
+      uint64_t(P.layers) * P.batch * win >= (uint64_t(1) << 31))
+    return 1;
+  static const bool off = [] {
+    const char* e = getenv("WGKV_SNAPKV_MMA_SYNC");
+    return e && e[0] == '1';
+  }();
+  if (off) return 1;
+  // tensor maps are encoded per call (cheap host work next to the passes)
+  CUtensorMap q1, q2, km;
+  const uint64_t dims[3] = {uint64_t(D), uint64_t(Hq), uint64_t(P.layers) * P.batch * win};
+  const uint64_t str[2] = {uint64_t(D), uint64_t(Hq) * D};
+  const uint32_t box1[3] = {64, uint32_t(G), uint32_t(128 / G)}, box2[3] = {64, uint32_t(G), uint32_t(kNC / G)};
+  if (!encode_3d_bf16(&q1, queries, dims, str, box1, true) || !encode_3d_bf16(&q2, queries, dims, str, box2, true) ||
+      !encode_2d_bf16(&km, P.k, D, uint64_t(P.total_blocks) * T, D, 64, uint32_t(T), true))
+    return WGKV_ECUDA;
+  SnTcArgs a{};
+  a.layer = layer;
+  a.B = P.batch;
+  a.Hk = Hk;
+  a.G = G;
+  a.win = win;
+  a.R = R;
+  a.T = T;
+  a.window_pages = P.window / T;
+  a.max_blocks = P.max_blocks_per_head;
+  a.max_tok = P.max_tokens_per_head;
+  a.block_table = P.block_table;
+  a.lengths = P.global_lengths;
+  a.scale = scale;
+  a.inv_win = 1.f / float(win);
+  a.rowml = rowml;
+  a.scores = scores;
+  a.err = P.err;
+  const int BH = P.batch * Hk;
+  // pass 2: each CTA takes every gridDim.x-th key tile of its head, about 4 tiles per CTA for the
+  // longest possible head
+  const int max_tiles = (P.max_tokens_per_head + kTK - 1) / kTK;
+  const dim3 g1((R + 255) / 256, BH), g2(max(1, (max_tiles + 3) / 4), BH);
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (D == 128) {
+    using L = SnL<128>;
+    if (dev < 64 && !attr[dev]) {
+      if (cudaFuncSetAttribute(snap_rowstats_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               L::kSmem1) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_scores_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               L::kSmem2) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_rowstats_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SnL<64>::kSmem1) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_scores_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SnL<64>::kSmem2) != cudaSuccess)
+        return WGKV_ECUDA;
+      attr[dev] = true;
+    }
+    snap_rowstats_tc_kernel<128><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
+    snap_scores_tc_kernel<128><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
+  } else {
+    using L = SnL<64>;
+    if (dev < 64 && !attr[dev]) {
+      if (cudaFuncSetAttribute(snap_rowstats_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SnL<128>::kSmem1) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_scores_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SnL<128>::kSmem2) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_rowstats_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               L::kSmem1) != cudaSuccess ||
+          cudaFuncSetAttribute(snap_scores_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               L::kSmem2) != cudaSuccess)
+        return WGKV_ECUDA;
+      attr[dev] = true;
+    }
+    snap_rowstats_tc_kernel<64><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
+    snap_scores_tc_kernel<64><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
+  }
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
+}  // namespace wgkv

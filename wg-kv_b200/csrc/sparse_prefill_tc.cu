@@ -131,7 +131,14 @@ WGKV_DEV void exp2_pair(int pi, uint64_t x2, float x0, float x1, float& p0, floa
     p0 = fast_exp2(x0);
     p1 = fast_exp2(x1);
   }
+#ifdef WGKV_PACK_INT
+  // round half up on the bit patterns (P is finite and >= 0), then one byte permute takes both upper
+  // halves: integer-pipe work instead of a conversion instruction per pair
+  const uint32_t a = __float_as_uint(p0) + 0x8000u, b = __float_as_uint(p1) + 0x8000u;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(packed) : "r"(a), "r"(b));
+#else
   packed = pack_bf16x2(p0, p1);
+#endif
 }
 
 struct TcParams {
@@ -370,6 +377,11 @@ __global__ void __launch_bounds__(Tc<D, NM, HV>::kThreads, 1)
     const float sc = p.scale_log2;
     const int qlim = min(q, p.L - 1);
     float m_used = -INFINITY, l = 0.f;
+#ifdef WGKV_PREFILL_PINGPONG
+    if constexpr (NM == 2 && HV == 1) {
+      if (t == 1 && n > 0) asm volatile("bar.arrive 9, 256;" ::: "memory");  // M-tile 0 goes first
+    }
+#endif
     for (int j = 0; j < n; ++j) {
       if (ok && !mbar_wait(&bar->sfull[t], j & 1)) { set_error(p.err, WGKV_ERR_TIMEOUT); ok = false; }
       if (quad == 0 && lane == 0 && hf == 0) { WGKV_TRACE(4 + t, j) }
@@ -441,6 +453,11 @@ __global__ void __launch_bounds__(Tc<D, NM, HV>::kThreads, 1)
           tmem_st32(trow + 128 + hf * kOC + c0, ov);
         }
       }
+#ifdef WGKV_PREFILL_PINGPONG
+      // the two M-tiles' exponential loops take turns (named barriers 9 / 10, 256 threads each), so
+      // one tile's exponentials run while the other tile's MMAs do
+      if constexpr (NM == 2 && HV == 1) asm volatile("bar.sync %0, 256;" ::"r"(9 + t) : "memory");
+#endif
       const float nbase = m_used == -INFINITY ? 0.f : -m_used;
       // p = 2^(s * scale - m): the scale-and-shift as paired FMAs, the exponential on the SFU (part
       // on the FMA pipe), the row sum as paired adds; each 32-key chunk of P goes to TMEM (packed
@@ -469,6 +486,11 @@ __global__ void __launch_bounds__(Tc<D, NM, HV>::kThreads, 1)
       f2_split(sa, s0_, s1_);
       f2_split(sb, s2_, s3_);
       l = l * alpha + ((s0_ + s1_) + (s2_ + s3_));
+#ifdef WGKV_PREFILL_PINGPONG
+      if constexpr (NM == 2 && HV == 1) {
+        if (t == 0 || j + 1 < n) asm volatile("bar.arrive %0, 256;" ::"r"(10 - t) : "memory");
+      }
+#endif
       if (quad == 0 && lane == 0 && t == 0 && hf == 0) { WGKV_TRACE(12, j) }
       // the P stores and any O rescale must land before the MMA reads them
       tmem_wait_st();
