@@ -238,16 +238,38 @@ struct SelectArgs {
   int* nb;              // [layers][BH][2]: pages before / after
 };
 
+// max-pooled scores of every head (odd kernel, padding kernel / 2) as ascending 32-bit keys,
+// one thread per position
+__global__ void __launch_bounds__(256) snap_pool_kernel(SelectArgs a) {
+  const wgkv_pool& P = a.P;
+  const int BH = P.batch * P.kv_heads, bh = blockIdx.y;
+  const int glen = P.global_lengths[int64_t(a.layer) * BH + bh];
+  const int p = blockIdx.x * 256 + threadIdx.x;
+  if (p >= glen || int(double(glen) * a.ratio) == 0) return;
+  const float* sc = a.scores + int64_t(bh) * a.max_tok;
+  const int pad = a.ks / 2, lo = max(0, p - pad), hi = min(glen - 1, p + pad);
+  float m = -INFINITY;
+  for (int q = lo; q <= hi; ++q) m = fmaxf(m, sc[q]);
+  reinterpret_cast<uint32_t*>(a.pooled)[int64_t(bh) * a.max_tok + p] = float_key(m);
+}
+
+constexpr int kSelThreads = 1024;
+constexpr int kSelWarps = kSelThreads / 32;
+
+// Per head: the n_ev-th smallest pooled key by four 8-bit radix passes (several keys in flight per
+// thread), then the in-place front compaction of the kept tokens in 1024-position chunks, each
+// moved in four rounds of 256 rows (four threads per row, the row's K and V parts in registers):
+// a round reads all its rows before any is written, and a kept token only moves to a lower
+// position, so no row is overwritten before it is read.
 template <int D>
-__global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectArgs a) {
-  extern __shared__ __align__(16) uint8_t sn_smem[];
-  uint4* stage = reinterpret_cast<uint4*>(sn_smem);  // [kSnThreads][2 * D / 8]
+__global__ void __launch_bounds__(kSelThreads) snap_select_compact_kernel(SelectArgs a) {
   const wgkv_pool& P = a.P;
   const int Hk = P.kv_heads, BH = P.batch * Hk, T = P.page;
   const int bh = blockIdx.x, tid = threadIdx.x;
   __shared__ int hist[256];
-  __shared__ int wsum[kSnWarps];
+  __shared__ int wsum[kSelWarps];
   __shared__ int s_bin, s_take;
+  __shared__ int dsts[kSelThreads];
   int* gl = P.global_lengths + int64_t(a.layer) * BH + bh;
   const int glen = *gl;
   const int nb_old = (glen + T - 1) / T;
@@ -257,26 +279,27 @@ __global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectA
     if (tid == 0) { nb[0] = nb_old; nb[1] = nb_old; }
     return;
   }
-  const float* sc = a.scores + int64_t(bh) * a.max_tok;
-  float* pl = a.pooled + int64_t(bh) * a.max_tok;
-  const int pad = a.ks / 2;
-  for (int p = tid; p < glen; p += kSnThreads) {
-    float m = -INFINITY;
-    for (int d = -pad; d <= pad; ++d)
-      if (p + d >= 0 && p + d < glen) m = fmaxf(m, sc[p + d]);
-    pl[p] = m;
-  }
-  __syncthreads();
+  const uint32_t* pk = reinterpret_cast<const uint32_t*>(a.pooled) + int64_t(bh) * a.max_tok;
   // n_ev-th smallest key, four 8-bit passes from the top byte
   int need = n_ev;
   uint32_t prefix = 0;
+  constexpr int kU = 4;  // keys in flight per thread
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = tid; i < 256; i += kSnThreads) hist[i] = 0;
+    for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
     __syncthreads();
-    for (int p = tid; p < glen; p += kSnThreads) {
-      const uint32_t k = float_key(pl[p]);
-      if (pass == 0 || (k >> (shift + 8)) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
+    for (int b0 = 0; b0 < glen; b0 += kU * kSelThreads) {
+      uint32_t kk[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int p = b0 + u * kSelThreads + tid;
+        kk[u] = p < glen ? __ldg(pk + p) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int p = b0 + u * kSelThreads + tid;
+        if (p < glen && (pass == 0 || (kk[u] >> (shift + 8)) == prefix)) atomicAdd(&hist[(kk[u] >> shift) & 0xFF], 1);
+      }
     }
     __syncthreads();
     if (tid == 0) {
@@ -294,40 +317,48 @@ __global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectA
     __syncthreads();
   }
   const uint32_t kth = prefix;  // evict keys < kth and the first `need` equal to it
-  // in-place compaction, chunks of kSnThreads positions: read the kept rows, barrier, write
   const int32_t* grow = P.block_table + (int64_t(a.layer) * BH + bh) * P.max_blocks_per_head + P.window / T;
-  constexpr int V = D / 8;
+  constexpr int V = D / 8;   // 16-byte vectors per row
+  constexpr int VP = V / 4;  // per thread (four threads per row)
   int eq_seen = 0, kept_base = 0;
-  for (int c0 = 0; c0 < glen; c0 += kSnThreads) {
+  for (int c0 = 0; c0 < glen; c0 += kSelThreads) {
     const int p = c0 + tid;
-    uint32_t k = 0;
-    if (p < glen) k = float_key(pl[p]);
+    const uint32_t k = p < glen ? __ldg(pk + p) : 0u;
     const int is_eq = p < glen && k == kth;
     int tot_eq;
-    const int eq_rank = eq_seen + block_excl_scan<kSnThreads>(is_eq, wsum, tot_eq);
+    const int eq_rank = eq_seen + block_excl_scan<kSelThreads>(is_eq, wsum, tot_eq);
     const int keep = p < glen && !(k < kth || (is_eq && eq_rank < need));
     int tot_keep;
-    const int dst = kept_base + block_excl_scan<kSnThreads>(keep, wsum, tot_keep);
-    if (keep) {
-      const int64_t row = int64_t(grow[p / T]) * T + p % T;
-      const uint4* kr = reinterpret_cast<const uint4*>(P.k + row * D);
-      const uint4* vr = reinterpret_cast<const uint4*>(P.v + row * D);
-      for (int c = 0; c < V; ++c) {
-        stage[tid * 2 * V + c] = kr[c];
-        stage[tid * 2 * V + V + c] = vr[c];
-      }
-    }
+    const int dst = kept_base + block_excl_scan<kSelThreads>(keep, wsum, tot_keep);
+    dsts[tid] = keep && dst != p ? dst : -1;
     __syncthreads();
-    if (keep && dst != p) {
-      const int64_t row = int64_t(grow[dst / T]) * T + dst % T;
-      uint4* kw = reinterpret_cast<uint4*>(P.k + row * D);
-      uint4* vw = reinterpret_cast<uint4*>(P.v + row * D);
-      for (int c = 0; c < V; ++c) {
-        kw[c] = stage[tid * 2 * V + c];
-        vw[c] = stage[tid * 2 * V + V + c];
+    for (int r0 = 0; r0 < kSelThreads && c0 + r0 < glen; r0 += 256) {
+      const int rl = r0 + (tid >> 2), part = tid & 3;
+      const int src = c0 + rl, d = dsts[rl];
+      uint4 kv[2 * VP];
+      if (d >= 0) {
+        const int64_t row = int64_t(__ldg(grow + src / T)) * T + src % T;
+        const uint4* kr = reinterpret_cast<const uint4*>(P.k + row * D) + part * VP;
+        const uint4* vr = reinterpret_cast<const uint4*>(P.v + row * D) + part * VP;
+#pragma unroll
+        for (int c = 0; c < VP; ++c) {
+          kv[c] = kr[c];
+          kv[VP + c] = vr[c];
+        }
       }
+      __syncthreads();
+      if (d >= 0) {
+        const int64_t row = int64_t(__ldg(grow + d / T)) * T + d % T;
+        uint4* kw = reinterpret_cast<uint4*>(P.k + row * D) + part * VP;
+        uint4* vw = reinterpret_cast<uint4*>(P.v + row * D) + part * VP;
+#pragma unroll
+        for (int c = 0; c < VP; ++c) {
+          kw[c] = kv[c];
+          vw[c] = kv[VP + c];
+        }
+      }
+      __syncthreads();
     }
-    __syncthreads();
     eq_seen += tot_eq;
     kept_base += tot_keep;
   }
@@ -341,7 +372,8 @@ __global__ void __launch_bounds__(kSnThreads) snap_select_compact_kernel(SelectA
 // ---- freed pages -> the free list, (layer, b, h) order; their table entries -> sentinel ----
 constexpr int kFreeThreads = 1024;
 
-__global__ void __launch_bounds__(kFreeThreads) snap_free_kernel(wgkv_pool P, const int* nb) {
+// (one CTA: each head's first free-list slot, the list's new length)
+__global__ void __launch_bounds__(kFreeThreads) snap_free_kernel(wgkv_pool P, const int* nb, int* offs) {
   const int N = P.layers * P.batch * P.kv_heads;
   const int per = (N + kFreeThreads - 1) / kFreeThreads;
   const int i0 = min(N, int(threadIdx.x) * per), i1 = min(N, i0 + per);
@@ -363,16 +395,24 @@ __global__ void __launch_bounds__(kFreeThreads) snap_free_kernel(wgkv_pool P, co
   }
   const int fc = *P.free_count;
   int off = fc + base + x - cnt;
-  const int sentinel = int(P.total_blocks - 1);
   for (int i = i0; i < i1; ++i) {
-    int32_t* row = P.block_table + int64_t(i) * P.max_blocks_per_head + P.window / P.page;
-    for (int j = nb[2 * i + 1]; j < nb[2 * i]; ++j) {
-      P.free_ids[off++] = row[j];
-      row[j] = sentinel;
-    }
+    offs[i] = off;
+    off += nb[2 * i] - nb[2 * i + 1];
   }
   __syncthreads();
   if (threadIdx.x == 0) *P.free_count = fc + tot;
+}
+
+// one CTA per head: its freed pages to the list from its slot on, their table entries -> sentinel
+__global__ void __launch_bounds__(128) snap_free_write_kernel(wgkv_pool P, const int* nb, const int* offs) {
+  const int i = blockIdx.x;
+  const int j0 = nb[2 * i + 1], j1 = nb[2 * i], off = offs[i];
+  int32_t* row = P.block_table + int64_t(i) * P.max_blocks_per_head + P.window / P.page;
+  const int sentinel = int(P.total_blocks - 1);
+  for (int j = j0 + threadIdx.x; j < j1; j += 128) {
+    P.free_ids[off + j - j0] = row[j];
+    row[j] = sentinel;
+  }
 }
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -383,6 +423,7 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 namespace wgkv {
 int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int win, int Hq, float scale,
                      float2* rowml, float* scores, cudaStream_t s);  // snapkv_tc.cu
+size_t snapkv_tc_rowml_splits(int max_tokens_per_head);                  // snapkv_tc.cu
 }
 
 using namespace wgkv;
@@ -391,8 +432,8 @@ extern "C" size_t wgkv_snapkv_workspace_size(const wgkv_pool* pool, int window, 
   if (!pool || pool->kv_heads <= 0) return 0;
   const size_t BH = size_t(pool->batch) * pool->kv_heads;
   const size_t R = size_t(window) * (q_heads / pool->kv_heads);
-  return round256(BH * R * 8) + 2 * round256(BH * size_t(pool->max_tokens_per_head) * 4) +
-         round256(size_t(pool->layers) * BH * 8);
+  return round256(BH * R * 8 * snapkv_tc_rowml_splits(pool->max_tokens_per_head)) + 2 * round256(BH * size_t(pool->max_tokens_per_head) * 4) +
+         round256(size_t(pool->layers) * BH * 8) + round256(size_t(pool->layers) * BH * 4);
 }
 
 extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries, int window, int q_heads,
@@ -417,8 +458,8 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
   a.R = int(R);
   a.scale = softmax_scale;
   a.rowml = reinterpret_cast<float2*>(ws);
-  a.scores = reinterpret_cast<float*>(ws + round256(size_t(BH) * R * 8));
   a.max_tok = pool->max_tokens_per_head;
+  a.scores = reinterpret_cast<float*>(ws + round256(size_t(BH) * R * 8 * snapkv_tc_rowml_splits(a.max_tok)));
   SelectArgs sa{};
   sa.P = *pool;
   sa.ks = kernel_size;
@@ -430,18 +471,6 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem_keys = size_t(kKeys) * (D + 8) * 2;
   const size_t smem_scores = smem_keys + kKeys * 4;
-  const size_t smem_stage = size_t(kSnThreads) * 2 * D * 2;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(snap_select_compact_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSnThreads * 2 * 64 * 2) != cudaSuccess ||
-        cudaFuncSetAttribute(snap_select_compact_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSnThreads * 2 * 128 * 2) != cudaSuccess)
-      return WGKV_ECUDA;
-    attr[dev] = true;
-  }
   const int max_chunks = (pool->max_tokens_per_head + kKeys - 1) / kKeys;
   for (int l = 0; l < pool->layers; ++l) {
     a.layer = l;
@@ -455,15 +484,19 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
         snap_rowstats_kernel<128><<<g1, kSnThreads, smem_keys, s>>>(a);
         snap_scores_kernel<128><<<g2, kSnThreads, smem_scores, s>>>(a);
       }
-      snap_select_compact_kernel<128><<<BH, kSnThreads, smem_stage, s>>>(sa);
+      snap_pool_kernel<<<dim3(max_chunks * kKeys / 256 + 1, BH), 256, 0, s>>>(sa);
+      snap_select_compact_kernel<128><<<BH, kSelThreads, 0, s>>>(sa);
     } else {
       if (tc == 1) {
         snap_rowstats_kernel<64><<<g1, kSnThreads, smem_keys, s>>>(a);
         snap_scores_kernel<64><<<g2, kSnThreads, smem_scores, s>>>(a);
       }
-      snap_select_compact_kernel<64><<<BH, kSnThreads, smem_stage, s>>>(sa);
+      snap_pool_kernel<<<dim3(max_chunks * kKeys / 256 + 1, BH), 256, 0, s>>>(sa);
+      snap_select_compact_kernel<64><<<BH, kSelThreads, 0, s>>>(sa);
     }
   }
-  snap_free_kernel<<<1, kFreeThreads, 0, s>>>(*pool, sa.nb);
+  int* offs = sa.nb + round256(size_t(pool->layers) * BH * 8) / 4;
+  snap_free_kernel<<<1, kFreeThreads, 0, s>>>(*pool, sa.nb, offs);
+  snap_free_write_kernel<<<pool->layers * BH, 128, 0, s>>>(*pool, sa.nb, offs);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }

@@ -13,8 +13,8 @@
 //           = row), keeps the running max and sum of exp.
 //   pass 2  key scores, transposed: the keys are the M dimension, so a thread owns a key and
 //           sees all window rows of its TMEM lane, and the max over the group and the sum over
-//           the window need no exchange between threads.  One CTA per (head, every gridDim.x-th
-//           128-key tile): S^T = K Q^T (M=128 keys, N=256 window rows per MMA, Q chunks streamed
+//           the window need no exchange between threads.  One CTA per (head, 16 consecutive
+//           128-key tiles): S^T = K Q^T (M=128 keys, N=256 window rows per MMA, Q chunks streamed
 //           by TMA through a 2-stage ring); the CTA's tiles go in pairs, one per warpgroup, each
 //           with its own 256-column TMEM slot, and both tiles of a pair share every Q chunk.
 //
@@ -30,6 +30,8 @@ namespace {
 constexpr int kTK = 128;       // keys per K tile
 constexpr int kNC = 256;       // window rows per pass-2 MMA
 constexpr int kMaxRows = 2048; // window rows per head (win x G) the pass-2 statistics table holds
+constexpr int kTilesPerCta = 16;  // pass 2: consecutive K tiles per CTA
+constexpr int kSplit = 32;     // pass 1: K tiles per CTA (a head's keys split over CTAs, merged in pass 2)
 
 template <int D>
 struct SnL {
@@ -50,7 +52,7 @@ struct SnTcArgs {
   const int32_t* block_table;
   const int32_t* lengths;
   float scale, inv_win;
-  float2* rowml;   // [BH][R] (max, sum)
+  float2* rowml;   // [split][BH][R] (max, sum) of each pass-1 key split
   float* scores;   // [BH][max_tok]
   int* err;
 };
@@ -75,6 +77,24 @@ WGKV_DEV void round_scaled2(float& x0, float& x1, uint64_t sc2) {
   p = pack_bf16x2(y0, y1);
   x0 = __uint_as_float(p << 16);
   x1 = __uint_as_float(p & 0xFFFF0000u);
+}
+
+// e^d = 2^(d log2 e) on the SFU for d = s - m <= 0: the argument's rounding error grows with |d|,
+// i.e. it is smallest for the terms that dominate the sums and maxima (relative error ~2^-22 there)
+WGKV_DEV float exp_sfu(float d) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d * 1.4426950408889634f));
+  return y;
+}
+WGKV_DEV float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+WGKV_DEV uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // K tile `kt` of a head (pages of T rows, T | 128) into `dst`: lane i issues page i's boxes.
@@ -115,7 +135,9 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
   if (glen <= 0) return;
   const int row0 = blockIdx.x * 256;
   const int nt = min(2, (a.R - row0 + 127) / 128);  // M-tiles of this CTA
-  const int n = (glen + kTK - 1) / kTK;
+  const int j0 = blockIdx.z * kSplit;                 // first K tile of this CTA's key split
+  if (j0 * kTK >= glen) return;
+  const int n = min(kSplit, (glen + kTK - 1) / kTK - j0);  // K tiles of this CTA
   const int nb = (glen + a.T - 1) / a.T;
   const int32_t* grow = a.block_table + (int64_t(a.layer) * a.B * a.Hk + bh) * a.max_blocks + a.window_pages;
 
@@ -154,7 +176,7 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
       if (!mbar_wait(&bar->kempty[s], ((j / kStg) & 1) ^ 1)) { ok = false; break; }
       if (lane == 0) mbar_arrive_expect_tx(&bar->kfull[s], L::kKTile);
       __syncwarp();
-      load_k_tile<D>(lane, sK + s * L::kKTile, &tmK, &bar->kfull[s], grow, nb, j, a.T);
+      load_k_tile<D>(lane, sK + s * L::kKTile, &tmK, &bar->kfull[s], grow, nb, j0 + j, a.T);
       __syncwarp();
     }
   } else if (warp == 1) {
@@ -203,29 +225,33 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
       if (lane == 0) mbar_arrive(&bar->sfree[t][u]);  // S is in registers: the slot may be refilled
 #pragma unroll
       for (int c = 0; c < kTK; c += 2) round_scaled2(sv[c], sv[c + 1], sc2);
-      const int lim = glen - j * kTK;  // valid keys of this tile
+      const int lim = glen - (j0 + j) * kTK;  // valid keys of this tile
       if (lim < kTK) {
 #pragma unroll
         for (int c = 0; c < kTK; ++c) sv[c] = c < lim ? sv[c] : -INFINITY;
       }
       float mx[8];
 #pragma unroll
-      for (int u8 = 0; u8 < 8; ++u8) mx[u8] = sv[u8];
+      for (int u8 = 0; u8 < 8; ++u8) mx[u8] = fmaxf(sv[u8], sv[u8 + 8]);
 #pragma unroll
-      for (int c = 8; c < kTK; c += 8)
+      for (int c = 16; c < kTK; c += 16)
 #pragma unroll
-        for (int u8 = 0; u8 < 8; ++u8) mx[u8] = fmaxf(mx[u8], sv[c + u8]);
-      float x = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        for (int u8 = 0; u8 < 8; ++u8) mx[u8] = max3f(mx[u8], sv[c + u8], sv[c + 8 + u8]);
+      float x = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const float nm = fmaxf(m, x);
-      float e[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t e0 = f2(0.f, 0.f), e1 = f2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < kTK; c += 4)
-#pragma unroll
-        for (int u4 = 0; u4 < 4; ++u4) e[u4] += expf(sv[c + u4] - nm);
-      l = l * expf(m - nm) + ((e[0] + e[1]) + (e[2] + e[3]));  // expf(-inf) = 0 on the first tile
+      for (int c = 0; c < kTK; c += 4) {
+        e0 = add2(e0, f2(exp_sfu(sv[c] - nm), exp_sfu(sv[c + 1] - nm)));
+        e1 = add2(e1, f2(exp_sfu(sv[c + 2] - nm), exp_sfu(sv[c + 3] - nm)));
+      }
+      float ea, eb, ec, ed;
+      f2_split(e0, ea, eb);
+      f2_split(e1, ec, ed);
+      l = l * expf(m - nm) + ((ea + eb) + (ec + ed));  // expf(-inf) = 0 on the first tile
       m = nm;
     }
-    if (ok && r < a.R) a.rowml[int64_t(bh) * a.R + r] = make_float2(m, l);
+    if (ok && r < a.R) a.rowml[(int64_t(blockIdx.z) * a.B * a.Hk + bh) * a.R + r] = make_float2(m, l);
   }
   if (!ok) set_error(a.err, WGKV_ERR_TIMEOUT);
   tc_fence_before();
@@ -243,7 +269,7 @@ struct Bars2 {
   uint32_t tmem;
 };
 
-template <int D>
+template <int D, int G>
 __global__ void __launch_bounds__(kSnTcThreads, 1)
     snap_scores_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           SnTcArgs a) {
@@ -258,15 +284,26 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
   const int bh = blockIdx.y, b = bh / a.Hk, h = bh - b * a.Hk;
   const int glen = a.lengths[int64_t(a.layer) * a.B * a.Hk + bh];
   const int ntile = (glen + kTK - 1) / kTK;
-  if (int(blockIdx.x) >= ntile) return;
-  const int ni = (ntile - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);  // tiles of this CTA
+  const int kt0 = blockIdx.x * kTilesPerCta;  // this CTA's tiles: kt0 .. kt0 + ni - 1
+  if (kt0 >= ntile) return;
+  const int ni = min(kTilesPerCta, ntile - kt0);
   const int nc = (a.R + kNC - 1) / kNC;                                             // Q chunks per tile
   const int nb = (glen + a.T - 1) / a.T;
   const int32_t* grow = a.block_table + (int64_t(a.layer) * a.B * a.Hk + bh) * a.max_blocks + a.window_pages;
 
+  // row statistics: merge pass 1's key splits (max, then the sums rescaled to it)
+  const int nsplit = (ntile + kSplit - 1) / kSplit;
+  const int64_t sstride = int64_t(a.B) * a.Hk * a.R;
   for (int r = tid; r < a.R; r += kSnTcThreads) {
-    const float2 ml = a.rowml[int64_t(bh) * a.R + r];
-    st[r] = make_float2(ml.x, 1.f / ml.y);
+    const float2* src = a.rowml + int64_t(bh) * a.R + r;
+    float m = -INFINITY;
+    for (int z = 0; z < nsplit; ++z) m = fmaxf(m, src[z * sstride].x);
+    float l = 0.f;
+    for (int z = 0; z < nsplit; ++z) {
+      const float2 ml = src[z * sstride];
+      l += ml.y * expf(ml.x - m);
+    }
+    st[r] = make_float2(m, 1.f / l);
   }
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -295,7 +332,7 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
     int q = 0;
     for (int pr = 0; 2 * pr < ni && ok; ++pr) {
       for (int w = 0; w < 2 && 2 * pr + w < ni; ++w) {
-        const int kt = blockIdx.x + (2 * pr + w) * gridDim.x;
+        const int kt = kt0 + 2 * pr + w;
         if (!mbar_wait(&bar->kempty[w], (pr & 1) ^ 1)) { ok = false; break; }
         if (lane == 0) mbar_arrive_expect_tx(&bar->kfull[w], L::kKTile);
         __syncwarp();
@@ -353,9 +390,8 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
     const int w = (warp - 4) / 4, quad = warp & 3;
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + w * 256;
     const uint64_t sc2 = f2(a.scale, a.scale);
-    const int G = a.G;
     for (int i = w; i < ni && ok; i += 2) {
-      const int kt = blockIdx.x + i * gridDim.x;
+      const int kt = kt0 + i;
       float acc = 0.f;
       for (int c = 0; c < nc; ++c) {
         const int uw = (i >> 1) * nc + c;
@@ -369,16 +405,20 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
 #pragma unroll
           for (int cc = 0; cc < 32; cc += 2) round_scaled2(sv[cc], sv[cc + 1], sc2);
           const int rb = c * kNC + p0;  // window row of sv[0]
-          // rows rb + g*G .. rb + g*G + G - 1 (G a power of two dividing 32) are the G query heads
-          // of one window position: max over them, then the sum over window positions
-          float gm = 0.f;
+          // rows rb + g*G .. rb + g*G + G - 1 are the G query heads of one window position: max over
+          // them, then the sum over window positions (rows past R, in a last partial piece, skipped)
+          const int gl = min(32, a.R - rb);
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) {
-            const float2 ml = st[rb + cc];
-            float pr = expf(sv[cc] - ml.x) * ml.y;
-            pr = rb + cc < a.R ? pr : 0.f;
-            gm = (cc & (G - 1)) == 0 ? pr : fmaxf(gm, pr);
-            if ((cc & (G - 1)) == G - 1) acc += gm;
+          for (int g0 = 0; g0 < 32; g0 += G) {
+            if (g0 < gl) {
+              float gm = 0.f;
+#pragma unroll
+              for (int e = 0; e < G; ++e) {
+                const float2 ml = st[rb + g0 + e];
+                gm = fmaxf(gm, exp_sfu(sv[g0 + e] - ml.x) * ml.y);
+              }
+              acc += gm;
+            }
           }
         }
         tc_fence_before();
@@ -398,6 +438,26 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
   }
 }
 
+template <int D, int G>
+int launch_passes(const CUtensorMap& q1, const CUtensorMap& q2, const CUtensorMap& km, const SnTcArgs& a, dim3 g1,
+                  dim3 g2, cudaStream_t s) {
+  using L = SnL<D>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(snap_rowstats_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem1) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(snap_scores_tc_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem2) !=
+            cudaSuccess)
+      return WGKV_ECUDA;
+    attr[dev] = true;
+  }
+  snap_rowstats_tc_kernel<D><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
+  snap_scores_tc_kernel<D, G><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
+  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+}
+
 }  // namespace
 
 // Per layer: the two score passes on the tensor cores.  Returns 1 when the shape does not fit
@@ -406,7 +466,7 @@ int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int
                      float2* rowml, float* scores, cudaStream_t s) {
   const int Hk = P.kv_heads, G = Hq / Hk, D = P.head_dim, T = P.page, R = win * G;
   if (D != 64 && D != 128) return 1;
-  if (32 % G || R % 16 || R > kMaxRows || T % 8 || kTK % T) return 1;
+  if (16 % G || R % 16 || R > kMaxRows || T % 8 || kTK % T) return 1;
   if ((reinterpret_cast<uintptr_t>(queries) | reinterpret_cast<uintptr_t>(P.k)) & 15) return 1;
   if (uint64_t(P.total_blocks) * T >= (uint64_t(1) << 31) ||
       uint64_t(P.layers) * P.batch * win >= (uint64_t(1) << 31))
@@ -443,47 +503,25 @@ int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int
   a.scores = scores;
   a.err = P.err;
   const int BH = P.batch * Hk;
-  // pass 2: each CTA takes every gridDim.x-th key tile of its head, about 4 tiles per CTA for the
-  // longest possible head
+  // pass 1: key splits of kSplit tiles; pass 2: kTilesPerCta consecutive key tiles per CTA
   const int max_tiles = (P.max_tokens_per_head + kTK - 1) / kTK;
-  const dim3 g1((R + 255) / 256, BH), g2(max(1, (max_tiles + 3) / 4), BH);
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (D == 128) {
-    using L = SnL<128>;
-    if (dev < 64 && !attr[dev]) {
-      if (cudaFuncSetAttribute(snap_rowstats_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               L::kSmem1) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_scores_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               L::kSmem2) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_rowstats_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SnL<64>::kSmem1) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_scores_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SnL<64>::kSmem2) != cudaSuccess)
-        return WGKV_ECUDA;
-      attr[dev] = true;
-    }
-    snap_rowstats_tc_kernel<128><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
-    snap_scores_tc_kernel<128><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
-  } else {
-    using L = SnL<64>;
-    if (dev < 64 && !attr[dev]) {
-      if (cudaFuncSetAttribute(snap_rowstats_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SnL<128>::kSmem1) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_scores_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SnL<128>::kSmem2) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_rowstats_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               L::kSmem1) != cudaSuccess ||
-          cudaFuncSetAttribute(snap_scores_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               L::kSmem2) != cudaSuccess)
-        return WGKV_ECUDA;
-      attr[dev] = true;
-    }
-    snap_rowstats_tc_kernel<64><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
-    snap_scores_tc_kernel<64><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
+  const dim3 g1((R + 255) / 256, BH, (max_tiles + kSplit - 1) / kSplit), g2((max_tiles + kTilesPerCta - 1) / kTilesPerCta, BH);
+  int st;
+  switch (G) {
+    case 1: st = D == 128 ? launch_passes<128, 1>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 1>(q1, q2, km, a, g1, g2, s); break;
+    case 2: st = D == 128 ? launch_passes<128, 2>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 2>(q1, q2, km, a, g1, g2, s); break;
+    case 4: st = D == 128 ? launch_passes<128, 4>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 4>(q1, q2, km, a, g1, g2, s); break;
+    case 8: st = D == 128 ? launch_passes<128, 8>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 8>(q1, q2, km, a, g1, g2, s); break;
+    case 16: st = D == 128 ? launch_passes<128, 16>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 16>(q1, q2, km, a, g1, g2, s); break;
+    default: return 1;
   }
-  return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
+  return st;
+}
+
+// Row-statistics entries pass 1 writes per (head, window row): one per key split of the longest head.
+size_t snapkv_tc_rowml_splits(int max_tokens_per_head) {
+  const int max_tiles = (max_tokens_per_head + kTK - 1) / kTK;
+  return size_t(max(1, (max_tiles + kSplit - 1) / kSplit));
 }
 
 }  // namespace wgkv

@@ -131,14 +131,7 @@ WGKV_DEV void exp2_pair(int pi, uint64_t x2, float x0, float x1, float& p0, floa
     p0 = fast_exp2(x0);
     p1 = fast_exp2(x1);
   }
-#ifdef WGKV_PACK_INT
-  // round half up on the bit patterns (P is finite and >= 0), then one byte permute takes both upper
-  // halves: integer-pipe work instead of a conversion instruction per pair
-  const uint32_t a = __float_as_uint(p0) + 0x8000u, b = __float_as_uint(p1) + 0x8000u;
-  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(packed) : "r"(a), "r"(b));
-#else
   packed = pack_bf16x2(p0, p1);
-#endif
 }
 
 struct TcParams {
