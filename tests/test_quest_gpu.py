@@ -91,10 +91,11 @@ def test_quest_golden_pipeline():
     assert np.array_equal(mn, z["final_quest_min"]) and np.array_equal(mx, z["final_quest_max"])
 
 
+@pytest.mark.parametrize("G,D", [(4, 128), (2, 64), (3, 128)])
 @pytest.mark.parametrize("budget", [64 + 400, 64 + 17, 64 + 16 * 500, 32])
-def test_quest_select_batched_matches_oracle(budget):
+def test_quest_select_batched_matches_oracle(budget, G, D):
     import wgkv
-    B, Hk, G, D, W, T, L = 2, 4, 4, 128, 64, 16, 3000
+    B, Hk, W, T, L = 2, 4, 64, 16, 3000
     Hq = Hk * G
     cache = SimpleNamespace()
     wgkv.init_pool(cache, layers=1, batch=B, kv_heads=Hk, head_dim=D, window=W, page=T,

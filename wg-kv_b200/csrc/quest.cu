@@ -52,78 +52,109 @@ WGKV_DEV int resolve_cur(const wgkv_pool& P, int cur) {
   return len < P.window ? len + 1 : P.window;
 }
 
-constexpr int kQsPagesPerCta = kQsThreads;  // one page per thread
+constexpr int kQsPagesPerCta = 64;  // 8 lanes per page, two pages per 8-lane group
 
-// Page scores of every head that has to rank its pages: one thread per page, streaming the page's
-// min / max rows with 16-byte loads against the group's queries in shared memory (broadcast reads);
-// writes order-preserving 16-bit keys to keys[bh][position].
-template <int D>
+WGKV_DEV uint64_t qf2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+WGKV_DEV uint64_t qadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Page scores of every head that has to rank its pages: eight lanes per page, each reading 16-byte
+// chunks sub, sub + 8, ... of the page's min and max rows (so the eight lanes read whole 128-byte
+// lines), against the group's queries in shared memory; the partial sums (even and odd dimensions
+// in an f32x2 pair) are added over the eight lanes.  Writes order-preserving 16-bit keys to
+// keys[bh][position].
+template <int D, int G>
 __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, int layer, int cur, const uint16_t* q,
-                                                                 int64_t q_sb, int Hq, int budget, uint16_t* keys,
+                                                                 int64_t q_sb, int budget, uint16_t* keys,
                                                                  int key_stride) {
+  constexpr int V = D / 8;    // 16-byte chunks per bound row
+  constexpr int CPL = V / 8;  // chunks per lane
+  constexpr int kPPI = 2;     // pages per 8-lane group
   const wgkv_pool& P = qa.P;
   const int Hk = P.kv_heads, BH = P.batch * Hk;
-  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk, G = Hq / Hk;
+  const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk;
   cur = resolve_cur(P, cur);
   const QuestHead H(P, layer, bh, cur, budget);
   const int p0 = blockIdx.x * kQsPagesPerCta;
   if (!H.ranks() || p0 >= H.full) return;
   // queries as bf16 pairs, and per pair a mask selecting min (q < 0) or max (q >= 0, -0 included)
-  __shared__ uint32_t q2[16 * D / 2];
-  __shared__ uint32_t neg[16 * D / 2];
+  __shared__ uint4 q2v[G * V], ngv[G * V];
+  uint32_t* q2 = reinterpret_cast<uint32_t*>(q2v);
+  uint32_t* ng = reinterpret_cast<uint32_t*>(ngv);
   const uint32_t* qh = reinterpret_cast<const uint32_t*>(q + int64_t(b) * q_sb + int64_t(h) * G * D);
   for (int i = threadIdx.x; i < G * D / 2; i += kQsThreads) {
     const uint32_t v = qh[i];
     q2[i] = v;
     const uint32_t lo_neg = (v & 0x8000u) && (v & 0x7FFFu) ? 0x0000FFFFu : 0u;
     const uint32_t hi_neg = (v & 0x80000000u) && (v & 0x7FFF0000u) ? 0xFFFF0000u : 0u;
-    neg[i] = lo_neg | hi_neg;
+    ng[i] = lo_neg | hi_neg;
   }
   __syncthreads();
-  const int pos = p0 + threadIdx.x;
-  if (pos >= H.full) return;
-  const int64_t pid = P.block_table[(int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page + pos];
-  const uint4* mn4 = reinterpret_cast<const uint4*>(P.quest_min + pid * D);
-  const uint4* mx4 = reinterpret_cast<const uint4*>(P.quest_max + pid * D);
-  float sum[16];
+  const int grp = threadIdx.x >> 3, sub = threadIdx.x & 7;
+  const int32_t* grow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head + P.window / P.page;
+  uint4 lo[kPPI][CPL], hi[kPPI][CPL];
+  int pos[kPPI];
 #pragma unroll
-  for (int g = 0; g < 16; ++g) sum[g] = 0.f;
-  constexpr int kC = 4;  // 16-byte chunks of each bound row in flight per pass
-#pragma unroll 1
-  for (int c0 = 0; c0 < D / 8; c0 += kC) {
-    uint4 lo[kC], hi[kC];
+  for (int u = 0; u < kPPI; ++u) {
+    pos[u] = p0 + u * (kQsThreads / 8) + grp;
+    const int64_t pid = pos[u] < H.full ? __ldg(grow + pos[u]) : 0;
+    const uint4* mn4 = reinterpret_cast<const uint4*>(P.quest_min + pid * D);
+    const uint4* mx4 = reinterpret_cast<const uint4*>(P.quest_max + pid * D);
 #pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      lo[c] = __ldg(mn4 + c0 + c);
-      hi[c] = __ldg(mx4 + c0 + c);
-    }
-#pragma unroll
-    for (int c = 0; c < kC; ++c) {
-      const uint32_t lw[4] = {lo[c].x, lo[c].y, lo[c].z, lo[c].w};
-      const uint32_t hw[4] = {hi[c].x, hi[c].y, hi[c].z, hi[c].w};
-#pragma unroll
-      for (int g = 0; g < 16; ++g) {
-        if (g >= G) break;
-        const int base = g * (D / 2) + (c0 + c) * 4;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t m = neg[base + e];
-          const uint32_t sel = (hw[e] & ~m) | (lw[e] & m);
-          // bf16(q * bound) for both halves: one round-to-nearest bf16x2 multiply
-          const __nv_bfloat162 pr = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&q2[base + e]),
-                                            *reinterpret_cast<const __nv_bfloat162*>(&sel));
-          const uint32_t pu = *reinterpret_cast<const uint32_t*>(&pr);
-          sum[g] += __uint_as_float(pu << 16);
-          sum[g] += __uint_as_float(pu & 0xffff0000u);
-        }
+    for (int i = 0; i < CPL; ++i) {
+      if (pos[u] < H.full) {
+        lo[u][i] = __ldg(mn4 + sub + 8 * i);
+        hi[u][i] = __ldg(mx4 + sub + 8 * i);
+      } else {
+        lo[u][i] = hi[u][i] = make_uint4(0, 0, 0, 0);
       }
     }
   }
-  float best = -INFINITY;
 #pragma unroll
-  for (int g = 0; g < 16; ++g)
-    if (g < G) best = fmaxf(best, bf16_round(sum[g]));
-  keys[int64_t(bh) * key_stride + pos] = uint16_t(score_key(f2bf(best)));
+  for (int u = 0; u < kPPI; ++u) {
+    uint64_t sum[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) sum[g] = qf2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = sub + 8 * i;
+      const uint32_t lw[4] = {lo[u][i].x, lo[u][i].y, lo[u][i].z, lo[u][i].w};
+      const uint32_t hw[4] = {hi[u][i].x, hi[u][i].y, hi[u][i].z, hi[u][i].w};
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint4 qq = q2v[g * V + c], nn = ngv[g * V + c];
+        const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w}, nw[4] = {nn.x, nn.y, nn.z, nn.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t sel = (hw[e] & ~nw[e]) | (lw[e] & nw[e]);
+          // bf16(q * bound) for both halves: one round-to-nearest bf16x2 multiply
+          const __nv_bfloat162 pr = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&qw[e]),
+                                            *reinterpret_cast<const __nv_bfloat162*>(&sel));
+          const uint32_t pu = *reinterpret_cast<const uint32_t*>(&pr);
+          sum[g] = qadd2(sum[g], qf2(__uint_as_float(pu << 16), __uint_as_float(pu & 0xffff0000u)));
+        }
+      }
+    }
+    float best = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float x, y;
+      asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(sum[g]));
+      float t = x + y;
+      t += __shfl_xor_sync(0xffffffff, t, 1);
+      t += __shfl_xor_sync(0xffffffff, t, 2);
+      t += __shfl_xor_sync(0xffffffff, t, 4);
+      best = fmaxf(best, bf16_round(t));
+    }
+    if (sub == 0 && pos[u] < H.full) keys[int64_t(bh) * key_stride + pos[u]] = uint16_t(score_key(f2bf(best)));
+  }
 }
 
 __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, int layer, int cur, int budget,
@@ -261,10 +292,30 @@ extern "C" int wgkv_quest_select(const wgkv_pool* pool, int layer, int cur_local
   const int ks = pool->max_blocks_per_head;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 g1((pool->max_blocks_per_head + kQsPagesPerCta - 1) / kQsPagesPerCta, BH);
-  if (pool->head_dim == 128)
-    quest_score_kernel<128><<<g1, kQsThreads, 0, s>>>(qa, layer, cur_local_len, q, q_sb, q_heads, token_budget, keys, ks);
-  else
-    quest_score_kernel<64><<<g1, kQsThreads, 0, s>>>(qa, layer, cur_local_len, q, q_sb, q_heads, token_budget, keys, ks);
+  const int G = q_heads / pool->kv_heads;
+#define WGKV_QS(DD, GG) quest_score_kernel<DD, GG><<<g1, kQsThreads, 0, s>>>(qa, layer, cur_local_len, q, q_sb, token_budget, keys, ks)
+#define WGKV_QS_D(GG) (pool->head_dim == 128 ? WGKV_QS(128, GG) : WGKV_QS(64, GG))
+  switch (G) {
+    case 1: WGKV_QS_D(1); break;
+    case 2: WGKV_QS_D(2); break;
+    case 3: WGKV_QS_D(3); break;
+    case 4: WGKV_QS_D(4); break;
+    case 5: WGKV_QS_D(5); break;
+    case 6: WGKV_QS_D(6); break;
+    case 7: WGKV_QS_D(7); break;
+    case 8: WGKV_QS_D(8); break;
+    case 9: WGKV_QS_D(9); break;
+    case 10: WGKV_QS_D(10); break;
+    case 11: WGKV_QS_D(11); break;
+    case 12: WGKV_QS_D(12); break;
+    case 13: WGKV_QS_D(13); break;
+    case 14: WGKV_QS_D(14); break;
+    case 15: WGKV_QS_D(15); break;
+    case 16: WGKV_QS_D(16); break;
+    default: return WGKV_EINVAL;
+  }
+#undef WGKV_QS_D
+#undef WGKV_QS
   quest_select_kernel<<<BH, kQsThreads, smem, s>>>(qa, layer, cur_local_len, token_budget, keys, ks, out_seqlens,
                                                    out_table, out_stride);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;

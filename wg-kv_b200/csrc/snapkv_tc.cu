@@ -398,13 +398,11 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
         if (!mbar_wait(&bar->sfull[w], uw & 1)) { ok = false; break; }
         tc_fence_after();
         const int ncols = min(kNC, a.R - c * kNC);
-        for (int p0 = 0; p0 < ncols; p0 += 32) {
-          float sv[32];
-          tmem_ld32(trow + p0, sv);
-          tmem_wait_ld();
+        // 32-column pieces, the next one's TMEM load in flight while this one is scored
+        auto score_piece = [&](float (&v)[32], int p0) {
 #pragma unroll
-          for (int cc = 0; cc < 32; cc += 2) round_scaled2(sv[cc], sv[cc + 1], sc2);
-          const int rb = c * kNC + p0;  // window row of sv[0]
+          for (int cc = 0; cc < 32; cc += 2) round_scaled2(v[cc], v[cc + 1], sc2);
+          const int rb = c * kNC + p0;  // window row of v[0]
           // rows rb + g*G .. rb + g*G + G - 1 are the G query heads of one window position: max over
           // them, then the sum over window positions (rows past R, in a last partial piece, skipped)
           const int gl = min(32, a.R - rb);
@@ -415,11 +413,23 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
 #pragma unroll
               for (int e = 0; e < G; ++e) {
                 const float2 ml = st[rb + g0 + e];
-                gm = fmaxf(gm, exp_sfu(sv[g0 + e] - ml.x) * ml.y);
+                gm = fmaxf(gm, exp_sfu(v[g0 + e] - ml.x) * ml.y);
               }
               acc += gm;
             }
           }
+        };
+        float sa[32], sb[32];
+        tmem_ld32(trow, sa);
+        tmem_wait_ld();
+        for (int p0 = 0; p0 < ncols; p0 += 64) {
+          if (p0 + 32 < ncols) tmem_ld32(trow + p0 + 32, sb);
+          score_piece(sa, p0);
+          tmem_wait_ld();
+          if (p0 + 32 >= ncols) break;
+          if (p0 + 64 < ncols) tmem_ld32(trow + p0 + 64, sa);
+          score_piece(sb, p0 + 32);
+          tmem_wait_ld();
         }
         tc_fence_before();
         __syncwarp();
