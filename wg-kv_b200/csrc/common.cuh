@@ -205,6 +205,38 @@ WGKV_DEV int block_excl_scan(int v, int* wsum, int& total) {
   return base + x - v;
 }
 
+// Radix-select step, run by one whole warp: walking the 256 bins of `hist` from the top (kDesc) or
+// the bottom, the bin that holds the need-th key and how many keys of it are still to take
+// (*take = need - keys in the bins before it).  Lane l sums 8 consecutive bins of the walk, a warp
+// scan finds the lane, that lane walks its 8 bins.  Past the end it stops at the last bin.
+template <bool kDesc>
+WGKV_DEV void warp_pick_bin(const int* hist, int need, int* bin_out, int* take_out) {
+  const int lane = threadIdx.x & 31;
+  int c[8], sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = hist[kDesc ? 255 - (lane * 8 + i) : lane * 8 + i];
+    sum += c[i];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffff, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const unsigned hit = __ballot_sync(0xffffffff, incl >= need);
+  const int L = hit ? __ffs(hit) - 1 : 31;
+  if (lane == L) {
+    int acc = incl - sum, i = 0;
+    for (; i < 7; ++i) {
+      if (acc + c[i] >= need) break;
+      acc += c[i];
+    }
+    *bin_out = kDesc ? 255 - (lane * 8 + i) : lane * 8 + i;
+    *take_out = need - acc;
+  }
+}
+
 WGKV_DEV void set_error(int* err, int code) {
   if (err) atomicOr(err, code);
 }

@@ -52,7 +52,11 @@ WGKV_DEV int resolve_cur(const wgkv_pool& P, int cur) {
   return len < P.window ? len + 1 : P.window;
 }
 
-constexpr int kQsPagesPerCta = 64;  // 8 lanes per page, two pages per 8-lane group
+#ifndef WGKV_QS_PPI
+#define WGKV_QS_PPI 4
+#endif
+constexpr int kQsPPI = WGKV_QS_PPI;                 // pages per 8-lane group
+constexpr int kQsPagesPerCta = kQsThreads / 8 * kQsPPI;
 
 WGKV_DEV uint64_t qf2(float lo, float hi) {
   uint64_t r;
@@ -76,7 +80,7 @@ __global__ void __launch_bounds__(kQsThreads) quest_score_kernel(QuestArgs qa, i
                                                                  int key_stride) {
   constexpr int V = D / 8;    // 16-byte chunks per bound row
   constexpr int CPL = V / 8;  // chunks per lane
-  constexpr int kPPI = 2;     // pages per 8-lane group
+  constexpr int kPPI = kQsPPI;
   const wgkv_pool& P = qa.P;
   const int Hk = P.kv_heads, BH = P.batch * Hk;
   const int bh = blockIdx.y, b = bh / Hk, h = bh - b * Hk;
@@ -197,15 +201,8 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
           if (pass == 0 || (k >> 8) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
         }
         __syncthreads();
-        if (tid == 0) {
-          int acc = 0, bin = 255;
-          for (; bin > 0; --bin) {
-            if (acc + hist[bin] >= need) break;
-            acc += hist[bin];
-          }
-          s_bin = bin;          // the bin holding the k-th key
-          s_take = need - acc;  // keys still to take from it
-        }
+        // the bin holding the k-th key, and the keys still to take from it
+        if (tid < 32) warp_pick_bin<true>(hist, need, &s_bin, &s_take);
         __syncthreads();
         prefix = pass == 0 ? uint32_t(s_bin) : (prefix << 8) | uint32_t(s_bin);
         need = s_take;

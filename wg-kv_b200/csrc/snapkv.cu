@@ -302,15 +302,7 @@ __global__ void __launch_bounds__(kSelThreads) snap_select_compact_kernel(Select
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      int acc = 0, bin = 0;
-      for (; bin < 255; ++bin) {
-        if (acc + hist[bin] >= need) break;
-        acc += hist[bin];
-      }
-      s_bin = bin;
-      s_take = need - acc;
-    }
+    if (tid < 32) warp_pick_bin<false>(hist, need, &s_bin, &s_take);
     __syncthreads();
     prefix = (prefix << 8) | uint32_t(s_bin);
     need = s_take;
