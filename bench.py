@@ -1059,7 +1059,7 @@ def quest_arm(args, rank, world, local_rank):
         wgkv.check_errors()
         after = int(cache.global_lengths.sum().item())
         evict_ms = e2.elapsed_time(e3)
-        flops = 2.0 * 2 * win * (Hq // Hk) * D * before * 2  # two passes of window-queries x keys
+        flops = 2.0 * 2 * win * (Hq // Hk) * D * before  # two passes of window-queries x keys (2 M N K each)
         snap = {"metric": "SnapKV eviction ms (all layers, whole pool)", "value": evict_ms, "unit": "ms",
                 "window": win, "evict_ratio": ratio, "kernel_size": ks, "tokens_before": before,
                 "tokens_after": after, "pages_freed": int(free_n.item()),
