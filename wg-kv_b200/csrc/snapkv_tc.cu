@@ -14,9 +14,10 @@
 //   pass 2  key scores, transposed: the keys are the M dimension, so a thread owns a key and
 //           sees all window rows of its TMEM lane, and the max over the group and the sum over
 //           the window need no exchange between threads.  One CTA per (head, 16 consecutive
-//           128-key tiles): S^T = K Q^T (M=128 keys, N=256 window rows per MMA, Q chunks streamed
-//           by TMA through a 2-stage ring); the CTA's tiles go in pairs, one per warpgroup, each
-//           with its own 256-column TMEM slot, and both tiles of a pair share every Q chunk.
+//           128-key tiles): S^T = K Q^T (M=128 keys, N=128 window rows per MMA, Q chunks streamed
+//           by TMA through a 2-stage ring); the CTA's tiles go in groups of four, one per compute
+//           warpgroup, each with its own 128-column TMEM slot, and the four tiles of a group share
+//           every Q chunk (four warps per scheduler hide the epilogue's latencies).
 //
 // Warp 0 issues the TMA loads (no multicast), lane 0 of warp 1 the MMAs; every wait is bounded and
 // a wait that runs out sets WGKV_ERR_TIMEOUT in the pool's error word (outputs are then undefined).
@@ -28,7 +29,8 @@ namespace wgkv {
 namespace {
 
 constexpr int kTK = 128;       // keys per K tile
-constexpr int kNC = 256;       // window rows per pass-2 MMA
+constexpr int kW2 = 4;                 // pass 2: compute warpgroups, each with its own TMEM slot
+constexpr int kNC2 = 512 / kW2;        // pass 2: window rows per MMA (N) = the slot's columns
 constexpr int kMaxRows = 2048; // window rows per head (win x G) the pass-2 statistics table holds
 constexpr int kTilesPerCta = 16;  // pass 2: consecutive K tiles per CTA
 constexpr int kSplit = 32;     // pass 1: K tiles per CTA (a head's keys split over CTAs, merged in pass 2)
@@ -39,13 +41,14 @@ struct SnL {
   static constexpr int kBox = 128 * 128;      // one box of 128 rows x 128 B
   static constexpr int kKTile = kDB * kBox;   // 128 keys
   static constexpr int kQ1 = kDB * kBox;      // pass 1: one 128-row M-tile of Q
-  static constexpr int kQ2 = kDB * 2 * kBox;  // pass 2: one 256-row chunk of Q
+  static constexpr int kQ2 = kDB * (kNC2 / 128) * kBox;  // pass 2: one kNC2-row chunk of Q
   static constexpr int kK1 = 3;               // pass-1 K stages
   static constexpr int kSmem1 = 2 * kQ1 + kK1 * kKTile + 256 + 1024;
-  static constexpr int kSmem2 = 2 * kKTile + 2 * kQ2 + kMaxRows * 8 + 256 + 1024;
+  static constexpr int kSmem2 = kW2 * kKTile + 2 * kQ2 + kMaxRows * 8 + 256 + 1024;
 };
 
-constexpr int kSnTcThreads = 384;  // warpgroup 0: TMA, MMA, two idle warps; two compute warpgroups
+constexpr int kSnTcThreads = 384;  // pass 1: warpgroup 0 (TMA, MMA, two idle warps), two compute warpgroups
+constexpr int kThreads2 = 128 + 128 * kW2;  // pass 2
 
 struct SnTcArgs {
   int layer, B, Hk, G, win, R, T, window_pages, max_blocks, max_tok;
@@ -264,20 +267,20 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
 
 // ============================== pass 2: key scores ==============================
 struct Bars2 {
-  uint64_t kfull[2], kempty[2], qfull[2], qempty[2];
-  uint64_t sfull[2], sfree[2];
+  uint64_t kfull[kW2], kempty[kW2], qfull[2], qempty[2];
+  uint64_t sfull[kW2], sfree[kW2];
   uint32_t tmem;
 };
 
 template <int D, int G>
-__global__ void __launch_bounds__(kSnTcThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
     snap_scores_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           SnTcArgs a) {
   using L = SnL<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
-  uint8_t* sQ = sm + 2 * L::kKTile;
+  uint8_t* sQ = sm + kW2 * L::kKTile;
   float2* st = reinterpret_cast<float2*>(sQ + 2 * L::kQ2);  // per window row: (max, 1 / sum)
   Bars2* bar = reinterpret_cast<Bars2*>(reinterpret_cast<uint8_t*>(st) + kMaxRows * 8);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -287,14 +290,14 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
   const int kt0 = blockIdx.x * kTilesPerCta;  // this CTA's tiles: kt0 .. kt0 + ni - 1
   if (kt0 >= ntile) return;
   const int ni = min(kTilesPerCta, ntile - kt0);
-  const int nc = (a.R + kNC - 1) / kNC;                                             // Q chunks per tile
+  const int nc = (a.R + kNC2 - 1) / kNC2;                                             // Q chunks per tile
   const int nb = (glen + a.T - 1) / a.T;
   const int32_t* grow = a.block_table + (int64_t(a.layer) * a.B * a.Hk + bh) * a.max_blocks + a.window_pages;
 
   // row statistics: merge pass 1's key splits (max, then the sums rescaled to it)
   const int nsplit = (ntile + kSplit - 1) / kSplit;
   const int64_t sstride = int64_t(a.B) * a.Hk * a.R;
-  for (int r = tid; r < a.R; r += kSnTcThreads) {
+  for (int r = tid; r < a.R; r += kThreads2) {
     const float2* src = a.rowml + int64_t(bh) * a.R + r;
     float m = -INFINITY;
     for (int z = 0; z < nsplit; ++z) m = fmaxf(m, src[z * sstride].x);
@@ -306,13 +309,15 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
     st[r] = make_float2(m, 1.f / l);
   }
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kW2; ++s) {
       mbar_init(&bar->kfull[s], 1);
       mbar_init(&bar->kempty[s], 1);
-      mbar_init(&bar->qfull[s], 1);
-      mbar_init(&bar->qempty[s], 1);
       mbar_init(&bar->sfull[s], 1);
       mbar_init(&bar->sfree[s], 4);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->qfull[s], 1);
+      mbar_init(&bar->qempty[s], 1);
     }
     fence_barrier_init();
   }
@@ -323,16 +328,16 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
   const uint32_t tmem = bar->tmem;
   bool ok = true;
   if (warp == 0) {
-    // ------- TMA producer: tiles in pairs (one per warpgroup); the pair's K, then Q chunks -------
+    // ------- TMA producer: tiles in groups (one per warpgroup); the group's K, then Q chunks -------
     if (lane == 0) {
       prefetch_tensormap(&tmQ);
       prefetch_tensormap(&tmK);
     }
     const int z0 = (a.layer * a.B + b) * a.win;
     int q = 0;
-    for (int pr = 0; 2 * pr < ni && ok; ++pr) {
-      for (int w = 0; w < 2 && 2 * pr + w < ni; ++w) {
-        const int kt = kt0 + 2 * pr + w;
+    for (int pr = 0; kW2 * pr < ni && ok; ++pr) {
+      for (int w = 0; w < kW2 && kW2 * pr + w < ni; ++w) {
+        const int kt = kt0 + kW2 * pr + w;
         if (!mbar_wait(&bar->kempty[w], (pr & 1) ^ 1)) { ok = false; break; }
         if (lane == 0) mbar_arrive_expect_tx(&bar->kfull[w], L::kKTile);
         __syncwarp();
@@ -345,24 +350,24 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
         if (lane == 0) {
           mbar_arrive_expect_tx(&bar->qfull[qs], L::kQ2);
           for (int d = 0; d < L::kDB; ++d)
-            tma_load_3d(sQ + qs * L::kQ2 + d * 2 * L::kBox, &tmQ, &bar->qfull[qs], d * 64, h * a.G,
-                        z0 + c * (kNC / a.G));
+            tma_load_3d(sQ + qs * L::kQ2 + d * (kNC2 / 128) * L::kBox, &tmQ, &bar->qfull[qs], d * 64, h * a.G,
+                        z0 + c * (kNC2 / a.G));
         }
         __syncwarp();
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: S^T = K Q^T per (tile, chunk), a pair's tiles alternating ----------------
+    // ---------------- MMA issuer: S^T = K Q^T per (tile, chunk), a group's tiles alternating ----------------
     if (lane == 0) {
       int q = 0;
-      for (int pr = 0; 2 * pr < ni && ok; ++pr) {
-        const int nw = min(2, ni - 2 * pr);  // tiles in this pair
+      for (int pr = 0; kW2 * pr < ni && ok; ++pr) {
+        const int nw = min(kW2, ni - kW2 * pr);  // tiles in this group
         for (int w = 0; w < nw; ++w)
           if (!mbar_wait(&bar->kfull[w], pr & 1)) { ok = false; break; }
         for (int c = 0; c < nc && ok; ++c, ++q) {
           const int qs = q & 1, uw = pr * nc + c;  // uw-th use of each warpgroup's slot
           if (!mbar_wait(&bar->qfull[qs], (q >> 1) & 1)) { ok = false; break; }
-          const int N = min(kNC, a.R - c * kNC);
+          const int N = min(kNC2, a.R - c * kNC2);
           const uint32_t idesc = umma_idesc_bf16(128, N, 0, 0);
           const uint32_t qa = smem_u32(sQ + qs * L::kQ2);
           for (int w = 0; w < nw; ++w) {
@@ -372,8 +377,8 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
 #pragma unroll
             for (int k = 0; k < D / 16; ++k) {
               const uint64_t da = umma_desc_sw128(ks + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
-              const uint64_t db = umma_desc_sw128(qa + (k >> 2) * 2 * L::kBox + (k & 3) * 32, 16, 1024);
-              umma_ss(tmem + w * 256, da, db, idesc, k > 0 ? 1u : 0u);
+              const uint64_t db = umma_desc_sw128(qa + (k >> 2) * (kNC2 / 128) * L::kBox + (k & 3) * 32, 16, 1024);
+              umma_ss(tmem + w * kNC2, da, db, idesc, k > 0 ? 1u : 0u);
             }
             umma_commit(&bar->sfull[w]);
           }
@@ -386,23 +391,23 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
-    // ---------------- scores: a thread per key, warpgroup w takes tile w of every pair ----------------
+    // ---------------- scores: a thread per key, warpgroup w takes tile w of every group ----------------
     const int w = (warp - 4) / 4, quad = warp & 3;
-    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + w * 256;
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + w * kNC2;
     const uint64_t sc2 = f2(a.scale, a.scale);
-    for (int i = w; i < ni && ok; i += 2) {
+    for (int i = w; i < ni && ok; i += kW2) {
       const int kt = kt0 + i;
       float acc = 0.f;
       for (int c = 0; c < nc; ++c) {
-        const int uw = (i >> 1) * nc + c;
+        const int uw = (i / kW2) * nc + c;
         if (!mbar_wait(&bar->sfull[w], uw & 1)) { ok = false; break; }
         tc_fence_after();
-        const int ncols = min(kNC, a.R - c * kNC);
+        const int ncols = min(kNC2, a.R - c * kNC2);
         // 32-column pieces, the next one's TMEM load in flight while this one is scored
         auto score_piece = [&](float (&v)[32], int p0) {
 #pragma unroll
           for (int cc = 0; cc < 32; cc += 2) round_scaled2(v[cc], v[cc + 1], sc2);
-          const int rb = c * kNC + p0;  // window row of v[0]
+          const int rb = c * kNC2 + p0;  // window row of v[0]
           // rows rb + g*G .. rb + g*G + G - 1 are the G query heads of one window position: max over
           // them, then the sum over window positions (rows past R, in a last partial piece, skipped)
           const int gl = min(32, a.R - rb);
@@ -464,7 +469,7 @@ int launch_passes(const CUtensorMap& q1, const CUtensorMap& q2, const CUtensorMa
     attr[dev] = true;
   }
   snap_rowstats_tc_kernel<D><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
-  snap_scores_tc_kernel<D, G><<<g2, kSnTcThreads, L::kSmem2, s>>>(q2, km, a);
+  snap_scores_tc_kernel<D, G><<<g2, kThreads2, L::kSmem2, s>>>(q2, km, a);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
 
@@ -490,7 +495,7 @@ int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int
   CUtensorMap q1, q2, km;
   const uint64_t dims[3] = {uint64_t(D), uint64_t(Hq), uint64_t(P.layers) * P.batch * win};
   const uint64_t str[2] = {uint64_t(D), uint64_t(Hq) * D};
-  const uint32_t box1[3] = {64, uint32_t(G), uint32_t(128 / G)}, box2[3] = {64, uint32_t(G), uint32_t(kNC / G)};
+  const uint32_t box1[3] = {64, uint32_t(G), uint32_t(128 / G)}, box2[3] = {64, uint32_t(G), uint32_t(kNC2 / G)};
   if (!encode_3d_bf16(&q1, queries, dims, str, box1, true) || !encode_3d_bf16(&q2, queries, dims, str, box2, true) ||
       !encode_2d_bf16(&km, P.k, D, uint64_t(P.total_blocks) * T, D, 64, uint32_t(T), true))
     return WGKV_ECUDA;
