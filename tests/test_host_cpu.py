@@ -37,7 +37,8 @@ def test_workspace_sizes():
     r256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
     splits = -(-(-(-1600 // 128)) // 32)  # row statistics per (head, row): one per 32-tile key split
     assert lib.wgkv_snapkv_workspace_size(ctypes.addressof(p), win, hq) == \
-        r256(BH * R * 8 * splits) + 2 * r256(BH * 1600 * 4) + r256(2 * BH * 8) + r256(2 * BH * 4)
+        r256(BH * R * 8 * splits) + 2 * r256(BH * 1600 * 4) + r256(2 * BH * 8) + 2 * r256(2 * BH * 4) + \
+        r256(2 * BH * ((1600 + 31) // 32 + 32) * 4)  # + keep bits per position (+ a chunk's slack)
     assert lib.wgkv_argmax_workspace_size(2, 128256) == 2 * (((128256 + 4095) // 4096) * 8 + 4) + 256
 
 

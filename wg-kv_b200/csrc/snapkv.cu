@@ -236,6 +236,9 @@ struct SelectArgs {
   float* pooled;        // [BH][max_tok]
   int max_tok;
   int* nb;              // [layers][BH][2]: pages before / after
+  int* olen;            // [layers][BH]: global length before the eviction
+  uint32_t* keep;       // [layers][BH][kw]: keep bit per position
+  int kw;               // keep words per head
 };
 
 // max-pooled scores of every head (odd kernel, padding kernel / 2) as ascending 32-bit keys,
@@ -257,24 +260,22 @@ constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 
 // Per head: the n_ev-th smallest pooled key by four 8-bit radix passes (several keys in flight per
-// thread), then the in-place front compaction of the kept tokens in 1024-position chunks, each
-// moved in four rounds of 256 rows (four threads per row, the row's K and V parts in registers):
-// a round reads all its rows before any is written, and a kept token only moves to a lower
-// position, so no row is overwritten before it is read.
-template <int D>
-__global__ void __launch_bounds__(kSelThreads) snap_select_compact_kernel(SelectArgs a) {
+// thread), then a keep bit per position (keys below it and the first `need` equal to it -- the
+// lowest positions -- are evicted) and the new length; the rows move later, for all layers at once.
+__global__ void __launch_bounds__(kSelThreads) snap_select_kernel(SelectArgs a) {
   const wgkv_pool& P = a.P;
   const int Hk = P.kv_heads, BH = P.batch * Hk, T = P.page;
-  const int bh = blockIdx.x, tid = threadIdx.x;
+  const int bh = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ int hist[256];
   __shared__ int wsum[kSelWarps];
   __shared__ int s_bin, s_take;
-  __shared__ int dsts[kSelThreads];
-  int* gl = P.global_lengths + int64_t(a.layer) * BH + bh;
+  const int64_t hi = int64_t(a.layer) * BH + bh;
+  int* gl = P.global_lengths + hi;
   const int glen = *gl;
   const int nb_old = (glen + T - 1) / T;
   const int n_ev = int(double(glen) * a.ratio);
-  int* nb = a.nb + (int64_t(a.layer) * BH + bh) * 2;
+  int* nb = a.nb + hi * 2;
+  if (tid == 0) a.olen[hi] = glen;
   if (n_ev == 0) {
     if (tid == 0) { nb[0] = nb_old; nb[1] = nb_old; }
     return;
@@ -309,22 +310,62 @@ __global__ void __launch_bounds__(kSelThreads) snap_select_compact_kernel(Select
     __syncthreads();
   }
   const uint32_t kth = prefix;  // evict keys < kth and the first `need` equal to it
-  const int32_t* grow = P.block_table + (int64_t(a.layer) * BH + bh) * P.max_blocks_per_head + P.window / T;
-  constexpr int V = D / 8;   // 16-byte vectors per row
-  constexpr int VP = V / 4;  // per thread (four threads per row)
-  int eq_seen = 0, kept_base = 0;
+  uint32_t* kb = a.keep + hi * a.kw;
+  int eq_seen = 0, kept = 0;
   for (int c0 = 0; c0 < glen; c0 += kSelThreads) {
     const int p = c0 + tid;
     const uint32_t k = p < glen ? __ldg(pk + p) : 0u;
     const int is_eq = p < glen && k == kth;
     int tot_eq;
     const int eq_rank = eq_seen + block_excl_scan<kSelThreads>(is_eq, wsum, tot_eq);
-    const int keep = p < glen && !(k < kth || (is_eq && eq_rank < need));
-    int tot_keep;
-    const int dst = kept_base + block_excl_scan<kSelThreads>(keep, wsum, tot_keep);
+    const bool keep = p < glen && !(k < kth || (is_eq && eq_rank < need));
+    const unsigned w = __ballot_sync(0xffffffff, keep);
+    if (lane == 0) kb[(c0 >> 5) + warp] = w;
+    kept += __syncthreads_count(keep);
+    eq_seen += tot_eq;
+  }
+  if (tid == 0) {
+    *gl = kept;
+    nb[0] = nb_old;
+    nb[1] = (kept + T - 1) / T;
+  }
+}
+
+// Every (layer, head) of the eviction at once: the in-place front compaction of the kept tokens in
+// 1024-position chunks, each moved in four rounds of 256 rows (four threads per row, the row's K
+// and V parts held in registers between the round's reads and its writes).  A round reads all its
+// rows before any is written, and a kept token only moves to a lower position, so no row is
+// overwritten before it is read.
+template <int D>
+__global__ void __launch_bounds__(kSelThreads) snap_compact_kernel(SelectArgs a) {
+  const wgkv_pool& P = a.P;
+  const int BH = P.batch * P.kv_heads, T = P.page;
+  const int64_t hi = blockIdx.x;  // layer * BH + bh
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int wsum[kSelWarps];
+  __shared__ int dsts[kSelThreads];
+  const int olen = a.olen[hi], nlen = P.global_lengths[hi];
+  if (nlen == olen) return;
+  const int32_t* grow = P.block_table + hi * P.max_blocks_per_head + P.window / T;
+  const uint32_t* kb = a.keep + hi * a.kw;
+  constexpr int V = D / 8;   // 16-byte vectors per row
+  constexpr int VP = V / 4;  // per thread (four threads per row)
+  int kept_base = 0;
+  for (int c0 = 0; c0 < olen; c0 += kSelThreads) {
+    const int p = c0 + tid;
+    const uint32_t w = p - lane < olen ? __ldg(kb + (c0 >> 5) + warp) : 0u;
+    const bool keep = p < olen && ((w >> lane) & 1u);
+    if (lane == 0) wsum[warp] = __popc(w);
+    __syncthreads();
+    int before = 0, tot = 0;
+    for (int i = 0; i < kSelWarps; ++i) {
+      before += i < warp ? wsum[i] : 0;
+      tot += wsum[i];
+    }
+    const int dst = kept_base + before + __popc(w & ((1u << lane) - 1u));
     dsts[tid] = keep && dst != p ? dst : -1;
     __syncthreads();
-    for (int r0 = 0; r0 < kSelThreads && c0 + r0 < glen; r0 += 256) {
+    for (int r0 = 0; r0 < kSelThreads && c0 + r0 < olen; r0 += 256) {
       const int rl = r0 + (tid >> 2), part = tid & 3;
       const int src = c0 + rl, d = dsts[rl];
       uint4 kv[2 * VP];
@@ -351,13 +392,7 @@ __global__ void __launch_bounds__(kSelThreads) snap_select_compact_kernel(Select
       }
       __syncthreads();
     }
-    eq_seen += tot_eq;
-    kept_base += tot_keep;
-  }
-  if (tid == 0) {
-    *gl = kept_base;
-    nb[0] = nb_old;
-    nb[1] = (kept_base + T - 1) / T;
+    kept_base += tot;
   }
 }
 
@@ -425,7 +460,8 @@ extern "C" size_t wgkv_snapkv_workspace_size(const wgkv_pool* pool, int window, 
   const size_t BH = size_t(pool->batch) * pool->kv_heads;
   const size_t R = size_t(window) * (q_heads / pool->kv_heads);
   return round256(BH * R * 8 * snapkv_tc_rowml_splits(pool->max_tokens_per_head)) + 2 * round256(BH * size_t(pool->max_tokens_per_head) * 4) +
-         round256(size_t(pool->layers) * BH * 8) + round256(size_t(pool->layers) * BH * 4);
+         round256(size_t(pool->layers) * BH * 8) + 2 * round256(size_t(pool->layers) * BH * 4) +
+         round256(size_t(pool->layers) * BH * ((size_t(pool->max_tokens_per_head) + 31) / 32 + kSelWarps) * 4);
 }
 
 extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries, int window, int q_heads,
@@ -460,6 +496,9 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
   sa.pooled = a.scores + round256(size_t(BH) * a.max_tok * 4) / 4;
   sa.max_tok = a.max_tok;
   sa.nb = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(sa.pooled) + round256(size_t(BH) * a.max_tok * 4));
+  sa.olen = sa.nb + (round256(size_t(pool->layers) * BH * 8) + round256(size_t(pool->layers) * BH * 4)) / 4;
+  sa.kw = (a.max_tok + 31) / 32 + kSelWarps;  // + slack: a chunk's words past the head's end
+  sa.keep = reinterpret_cast<uint32_t*>(sa.olen + round256(size_t(pool->layers) * BH * 4) / 4);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem_keys = size_t(kKeys) * (D + 8) * 2;
   const size_t smem_scores = smem_keys + kKeys * 4;
@@ -477,16 +516,21 @@ extern "C" int wgkv_snapkv_evict(const wgkv_pool* pool, const uint16_t* queries,
         snap_scores_kernel<128><<<g2, kSnThreads, smem_scores, s>>>(a);
       }
       snap_pool_kernel<<<dim3(max_chunks * kKeys / 256 + 1, BH), 256, 0, s>>>(sa);
-      snap_select_compact_kernel<128><<<BH, kSelThreads, 0, s>>>(sa);
+      snap_select_kernel<<<BH, kSelThreads, 0, s>>>(sa);
     } else {
       if (tc == 1) {
         snap_rowstats_kernel<64><<<g1, kSnThreads, smem_keys, s>>>(a);
         snap_scores_kernel<64><<<g2, kSnThreads, smem_scores, s>>>(a);
       }
       snap_pool_kernel<<<dim3(max_chunks * kKeys / 256 + 1, BH), 256, 0, s>>>(sa);
-      snap_select_compact_kernel<64><<<BH, kSelThreads, 0, s>>>(sa);
+      snap_select_kernel<<<BH, kSelThreads, 0, s>>>(sa);
     }
   }
+  // the rows of every layer move in one launch (one CTA per (layer, head)), then the freed pages
+  if (D == 128)
+    snap_compact_kernel<128><<<pool->layers * BH, kSelThreads, 0, s>>>(sa);
+  else
+    snap_compact_kernel<64><<<pool->layers * BH, kSelThreads, 0, s>>>(sa);
   int* offs = sa.nb + round256(size_t(pool->layers) * BH * 8) / 4;
   snap_free_kernel<<<1, kFreeThreads, 0, s>>>(*pool, sa.nb, offs);
   snap_free_write_kernel<<<pool->layers * BH, 128, 0, s>>>(*pool, sa.nb, offs);
