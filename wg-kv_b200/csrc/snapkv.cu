@@ -14,7 +14,9 @@
 // Kernels (per layer): row statistics and key scores on the tensor cores (snapkv_tc.cu) where the
 // shape fits them, else here on mma.sync m16n8k16 (row statistics: online max / sum over all
 // keys, one CTA per 128 window rows; key scores: one CTA per 64-key chunk, all window rows);
-// select + compact (one CTA per head).  After all layers: free-list append (one CTA).
+// max-pooling (one grid), selection (one CTA per head: radix bottom-k, keep bits, new length).
+// After all layers: the compaction of every (layer, head) in one launch, then the free-list slots
+// (one CTA) and the freed pages (one CTA per head).
 #include "common.cuh"
 
 namespace wgkv {
