@@ -6,11 +6,12 @@
 // there: q . k accumulated in fp32 and rounded to bf16, times the scale rounded to bf16 again,
 // then an fp32 softmax (expf, online max / sum in 128-key steps).
 //
-//   pass 1  row statistics.  One CTA per (head, 256 window rows): two M-tiles of 128 rows (Q
-//           resident in shared memory), K tiles of 128 keys streamed by TMA (one box per page
-//           and 64 columns) through a 3-stage ring; S = Q K^T (M=128, N=128) into a double-
-//           buffered TMEM slot per M-tile; one warpgroup per M-tile, a thread per row (TMEM lane
-//           = row), keeps the running max and sum of exp.
+//   pass 1  row statistics.  One CTA per (head, 512 window rows, 32 K tiles): four M-tiles of 128
+//           rows (Q resident in shared memory), K tiles of 128 keys streamed by TMA (one box per
+//           page and 64 columns) through a 3-stage ring; S = Q K^T (M=128, N=128) into a TMEM slot
+//           per M-tile; one warpgroup per M-tile, a thread per row (TMEM lane = row), keeps the
+//           running max and sum of exp over the tile's two 64-key halves (the slot is refilled
+//           while the second half is scored).  Pass 2 merges the key splits.
 //   pass 2  key scores, transposed: the keys are the M dimension, so a thread owns a key and
 //           sees all window rows of its TMEM lane, and the max over the group and the sum over
 //           the window need no exchange between threads.  One CTA per (head, 16 consecutive
@@ -19,7 +20,7 @@
 //           warpgroup, each with its own 128-column TMEM slot, and the four tiles of a group share
 //           every Q chunk (four warps per scheduler hide the epilogue's latencies).
 //
-// Warp 0 issues the TMA loads (no multicast), lane 0 of warp 1 the MMAs; every wait is bounded and
+// Warp 0 issues the TMA loads (no multicast), lane 0 of warp 1 the MMAs (warps 2-3 idle); every wait is bounded and
 // a wait that runs out sets WGKV_ERR_TIMEOUT in the pool's error word (outputs are then undefined).
 #include "common.cuh"
 #include "runtime.h"
@@ -29,6 +30,7 @@ namespace wgkv {
 namespace {
 
 constexpr int kTK = 128;       // keys per K tile
+constexpr int kW1 = 4;                 // pass 1: M-tiles (compute warpgroups, TMEM slots) per CTA
 constexpr int kW2 = 4;                 // pass 2: compute warpgroups, each with its own TMEM slot
 constexpr int kNC2 = 512 / kW2;        // pass 2: window rows per MMA (N) = the slot's columns
 constexpr int kMaxRows = 2048; // window rows per head (win x G) the pass-2 statistics table holds
@@ -43,12 +45,12 @@ struct SnL {
   static constexpr int kQ1 = kDB * kBox;      // pass 1: one 128-row M-tile of Q
   static constexpr int kQ2 = kDB * (kNC2 / 128) * kBox;  // pass 2: one kNC2-row chunk of Q
   static constexpr int kK1 = 3;               // pass-1 K stages
-  static constexpr int kSmem1 = 2 * kQ1 + kK1 * kKTile + 256 + 1024;
+  static constexpr int kSmem1 = kW1 * kQ1 + kK1 * kKTile + 256 + 1024;
   static constexpr int kSmem2 = kW2 * kKTile + 2 * kQ2 + kMaxRows * 8 + 256 + 1024;
 };
 
-constexpr int kSnTcThreads = 384;  // pass 1: warpgroup 0 (TMA, MMA, two idle warps), two compute warpgroups
 constexpr int kThreads2 = 128 + 128 * kW2;  // pass 2
+constexpr int kThreads1 = 128 + 128 * kW1;  // pass 1
 
 struct SnTcArgs {
   int layer, B, Hk, G, win, R, T, window_pages, max_blocks, max_tok;
@@ -118,26 +120,51 @@ WGKV_DEV void load_k_tile(int lane, uint8_t* dst, const CUtensorMap* tm, uint64_
 struct Bars1 {
   uint64_t qfull;
   uint64_t kfull[SnL<128>::kK1], kempty[SnL<128>::kK1];
-  uint64_t sfull[2][2], sfree[2][2];
+  uint64_t sfull[kW1], sfree[kW1];
   uint32_t tmem;
 };
 
+// running max / sum of e^(s - max) over 64 more scores of a row (masked ones are -inf)
+WGKV_DEV void rowstats_update(float (&sv)[64], float& m, float& l) {
+  float mx[8];
+#pragma unroll
+  for (int u8 = 0; u8 < 8; ++u8) mx[u8] = fmaxf(sv[u8], sv[u8 + 8]);
+#pragma unroll
+  for (int c = 16; c < 64; c += 16)
+#pragma unroll
+    for (int u8 = 0; u8 < 8; ++u8) mx[u8] = max3f(mx[u8], sv[c + u8], sv[c + 8 + u8]);
+  const float x = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+  const float nm = fmaxf(m, x);
+  if (nm == -INFINITY) return;  // nothing visible yet
+  uint64_t e0 = f2(0.f, 0.f), e1 = f2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 64; c += 4) {
+    e0 = add2(e0, f2(exp_sfu(sv[c] - nm), exp_sfu(sv[c + 1] - nm)));
+    e1 = add2(e1, f2(exp_sfu(sv[c + 2] - nm), exp_sfu(sv[c + 3] - nm)));
+  }
+  float ea, eb, ec, ed;
+  f2_split(e0, ea, eb);
+  f2_split(e1, ec, ed);
+  l = l * expf(m - nm) + ((ea + eb) + (ec + ed));  // expf(-inf) = 0 on the first scores
+  m = nm;
+}
+
 template <int D>
-__global__ void __launch_bounds__(kSnTcThreads, 1)
+__global__ void __launch_bounds__(kThreads1, 1)
     snap_rowstats_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             SnTcArgs a) {
   using L = SnL<D>;
   constexpr int kStg = L::kK1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = sm + 2 * L::kQ1;
+  uint8_t* sK = sm + kW1 * L::kQ1;
   Bars1* bar = reinterpret_cast<Bars1*>(sK + kStg * L::kKTile);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / a.Hk, h = bh - b * a.Hk;
   const int glen = a.lengths[int64_t(a.layer) * a.B * a.Hk + bh];
   if (glen <= 0) return;
-  const int row0 = blockIdx.x * 256;
-  const int nt = min(2, (a.R - row0 + 127) / 128);  // M-tiles of this CTA
+  const int row0 = blockIdx.x * 128 * kW1;
+  const int nt = min(kW1, (a.R - row0 + 127) / 128);  // M-tiles of this CTA
   const int j0 = blockIdx.z * kSplit;                 // first K tile of this CTA's key split
   if (j0 * kTK >= glen) return;
   const int n = min(kSplit, (glen + kTK - 1) / kTK - j0);  // K tiles of this CTA
@@ -150,11 +177,10 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
       mbar_init(&bar->kfull[s], 1);
       mbar_init(&bar->kempty[s], 1);
     }
-    for (int t = 0; t < 2; ++t)
-      for (int u = 0; u < 2; ++u) {
-        mbar_init(&bar->sfull[t][u], 1);
-        mbar_init(&bar->sfree[t][u], 4);
-      }
+    for (int t = 0; t < kW1; ++t) {
+      mbar_init(&bar->sfull[t], 1);
+      mbar_init(&bar->sfree[t], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc<512>(&bar->tmem);
@@ -188,20 +214,20 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
       const uint32_t idesc = umma_idesc_bf16(128, kTK, 0, 0);
       if (!mbar_wait(&bar->qfull, 0)) ok = false;
       for (int j = 0; j < n && ok; ++j) {
-        const int s = j % kStg, u = j & 1;
+        const int s = j % kStg;
         if (!mbar_wait(&bar->kfull[s], (j / kStg) & 1)) { ok = false; break; }
         const uint32_t ks = smem_u32(sK + s * L::kKTile);
         for (int t = 0; t < nt; ++t) {
-          if (!mbar_wait(&bar->sfree[t][u], ((j >> 1) & 1) ^ 1)) { ok = false; break; }
+          if (!mbar_wait(&bar->sfree[t], (j & 1) ^ 1)) { ok = false; break; }
           tc_fence_after();
           const uint32_t qt = smem_u32(sm + t * L::kQ1);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint64_t da = umma_desc_sw128(qt + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
             const uint64_t db = umma_desc_sw128(ks + (k >> 2) * L::kBox + (k & 3) * 32, 16, 1024);
-            umma_ss(tmem + t * 256 + u * 128, da, db, idesc, k > 0 ? 1u : 0u);
+            umma_ss(tmem + t * 128, da, db, idesc, k > 0 ? 1u : 0u);
           }
-          umma_commit(&bar->sfull[t][u]);
+          umma_commit(&bar->sfull[t]);
         }
         if (!ok) break;
         umma_commit(&bar->kempty[s]);
@@ -212,47 +238,32 @@ __global__ void __launch_bounds__(kSnTcThreads, 1)
     // ---------------- row statistics: a thread per window row ----------------
     const int t = (warp - 4) / 4, quad = warp & 3;
     const int r = row0 + t * 128 + quad * 32 + lane;
-    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 256;
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16) + t * 128;
     const uint64_t sc2 = f2(a.scale, a.scale);
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < n; ++j) {
-      const int u = j & 1;
-      if (!mbar_wait(&bar->sfull[t][u], (j >> 1) & 1)) { ok = false; break; }
+      if (!mbar_wait(&bar->sfull[t], j & 1)) { ok = false; break; }
       tc_fence_after();
-      float sv[kTK];
-#pragma unroll
-      for (int c = 0; c < kTK; c += 32) tmem_ld32(trow + u * 128 + c, sv + c);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->sfree[t][u]);  // S is in registers: the slot may be refilled
-#pragma unroll
-      for (int c = 0; c < kTK; c += 2) round_scaled2(sv[c], sv[c + 1], sc2);
       const int lim = glen - (j0 + j) * kTK;  // valid keys of this tile
-      if (lim < kTK) {
+      // the tile's two 64-key halves in turn; the slot is released once the second is loaded
+      for (int hf = 0; hf < 2; ++hf) {
+        float sv[64];
+        tmem_ld32(trow + hf * 64, sv);
+        tmem_ld32(trow + hf * 64 + 32, sv + 32);
+        tmem_wait_ld();
+        if (hf == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->sfree[t]);
+        }
 #pragma unroll
-        for (int c = 0; c < kTK; ++c) sv[c] = c < lim ? sv[c] : -INFINITY;
+        for (int c = 0; c < 64; c += 2) round_scaled2(sv[c], sv[c + 1], sc2);
+        if (lim - hf * 64 < 64) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) sv[c] = c < lim - hf * 64 ? sv[c] : -INFINITY;
+        }
+        rowstats_update(sv, m, l);
       }
-      float mx[8];
-#pragma unroll
-      for (int u8 = 0; u8 < 8; ++u8) mx[u8] = fmaxf(sv[u8], sv[u8 + 8]);
-#pragma unroll
-      for (int c = 16; c < kTK; c += 16)
-#pragma unroll
-        for (int u8 = 0; u8 < 8; ++u8) mx[u8] = max3f(mx[u8], sv[c + u8], sv[c + 8 + u8]);
-      float x = max3f(max3f(mx[0], mx[1], mx[2]), max3f(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      const float nm = fmaxf(m, x);
-      uint64_t e0 = f2(0.f, 0.f), e1 = f2(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < kTK; c += 4) {
-        e0 = add2(e0, f2(exp_sfu(sv[c] - nm), exp_sfu(sv[c + 1] - nm)));
-        e1 = add2(e1, f2(exp_sfu(sv[c + 2] - nm), exp_sfu(sv[c + 3] - nm)));
-      }
-      float ea, eb, ec, ed;
-      f2_split(e0, ea, eb);
-      f2_split(e1, ec, ed);
-      l = l * expf(m - nm) + ((ea + eb) + (ec + ed));  // expf(-inf) = 0 on the first tile
-      m = nm;
     }
     if (ok && r < a.R) a.rowml[(int64_t(blockIdx.z) * a.B * a.Hk + bh) * a.R + r] = make_float2(m, l);
   }
@@ -468,7 +479,7 @@ int launch_passes(const CUtensorMap& q1, const CUtensorMap& q2, const CUtensorMa
       return WGKV_ECUDA;
     attr[dev] = true;
   }
-  snap_rowstats_tc_kernel<D><<<g1, kSnTcThreads, L::kSmem1, s>>>(q1, km, a);
+  snap_rowstats_tc_kernel<D><<<g1, kThreads1, L::kSmem1, s>>>(q1, km, a);
   snap_scores_tc_kernel<D, G><<<g2, kThreads2, L::kSmem2, s>>>(q2, km, a);
   return cudaGetLastError() == cudaSuccess ? WGKV_OK : WGKV_ECUDA;
 }
@@ -520,7 +531,7 @@ int snapkv_scores_tc(const wgkv_pool& P, int layer, const uint16_t* queries, int
   const int BH = P.batch * Hk;
   // pass 1: key splits of kSplit tiles; pass 2: kTilesPerCta consecutive key tiles per CTA
   const int max_tiles = (P.max_tokens_per_head + kTK - 1) / kTK;
-  const dim3 g1((R + 255) / 256, BH, (max_tiles + kSplit - 1) / kSplit), g2((max_tiles + kTilesPerCta - 1) / kTilesPerCta, BH);
+  const dim3 g1((R + 128 * kW1 - 1) / (128 * kW1), BH, (max_tiles + kSplit - 1) / kSplit), g2((max_tiles + kTilesPerCta - 1) / kTilesPerCta, BH);
   int st;
   switch (G) {
     case 1: st = D == 128 ? launch_passes<128, 1>(q1, q2, km, a, g1, g2, s) : launch_passes<64, 1>(q1, q2, km, a, g1, g2, s); break;
