@@ -176,9 +176,10 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
   cur = resolve_cur(P, cur);
   const QuestHead H(P, layer, bh, cur, budget);
   const int local_blocks = H.local_blocks, full = H.full, full_cap = H.full_cap;
-  const int32_t* trow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head;
-  const int32_t* grow = trow + W / T;
-  int32_t* orow = out_tab + int64_t(bh) * out_stride;
+  // the pool's table is only read here and the output table only written: no aliasing
+  const int32_t* __restrict__ trow = P.block_table + (int64_t(layer) * BH + bh) * P.max_blocks_per_head;
+  const int32_t* __restrict__ grow = trow + W / T;
+  int32_t* __restrict__ orow = out_tab + int64_t(bh) * out_stride;
   for (int i = tid; i < local_blocks; i += kQsThreads) orow[i] = trow[i];
   int nsel = 0;
   if (full_cap > 0 && full > 0) {
@@ -223,10 +224,22 @@ __global__ void __launch_bounds__(kQsThreads) quest_select_kernel(QuestArgs qa, 
         r += k == kth;
       }
       int base = block_excl_scan<kQsThreads>(cnt, wsum, tot);
-      for (int i = i0, r = eq_rank; i < i1; ++i) {
-        const uint32_t k = keys[i];
-        if (k > kth || (k == kth && r < need)) orow[local_blocks + base++] = grow[i];
-        r += k == kth;
+      // this thread's chosen pages: their table entries loaded together, then stored in order
+      constexpr int kB = 8;
+      for (int c0 = i0, r = eq_rank; c0 < i1; c0 += kB) {
+        int32_t pid[kB];
+        bool take[kB];
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          const int i = c0 + u;
+          const uint32_t k = i < i1 ? keys[i] : 0u;
+          take[u] = i < i1 && (k > kth || (k == kth && r < need));
+          r += i < i1 && k == kth;
+          pid[u] = take[u] ? __ldg(grow + i) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < kB; ++u)
+          if (take[u]) orow[local_blocks + base++] = pid[u];
       }
       nsel = full_cap;
     }
