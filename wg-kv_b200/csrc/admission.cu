@@ -761,18 +761,29 @@ __global__ void __launch_bounds__(kDgaThreads) decode_gate_append_kernel(PoolArg
   float acc_out = 0.f;
   for (int j = tid; j < g.inner; j += kDgaThreads) {
     const uint4* wr = reinterpret_cast<const uint4*>(w1h + int64_t(j) * g.I);
+    const float b1j = bf2f(__ldg(g.b1 + h * g.inner + j)), w2j = bf2f(__ldg(g.w2 + h * g.inner + j));
     float s = 0.f;
-    for (int c = 0; c < g.I / 8; ++c) {
-      const uint4 w = __ldg(wr + c);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    // the row's 16-byte chunks in batches of 8, each batch's loads issued before its FMAs (the
+    // products are still summed in element order)
+    constexpr int kWB = 8;
+    for (int c0 = 0; c0 < g.I / 8; c0 += kWB) {
+      uint4 wb[kWB];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        s = fmaf(xs[c * 8 + 2 * e], __uint_as_float(ww[e] << 16), s);
-        s = fmaf(xs[c * 8 + 2 * e + 1], __uint_as_float(ww[e] & 0xffff0000u), s);
+      for (int u = 0; u < kWB; ++u) wb[u] = c0 + u < g.I / 8 ? __ldg(wr + c0 + u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kWB; ++u) {
+        if (c0 + u >= g.I / 8) break;
+        const int c = c0 + u;
+        const uint32_t ww[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s = fmaf(xs[c * 8 + 2 * e], __uint_as_float(ww[e] << 16), s);
+          s = fmaf(xs[c * 8 + 2 * e + 1], __uint_as_float(ww[e] & 0xffff0000u), s);
+        }
       }
     }
-    const float hb = gate_hidden(s, bf2f(g.b1[h * g.inner + j]), g.act);
-    acc_out += bf16_round(act_fn(hb, g.act)) * bf2f(g.w2[h * g.inner + j]);
+    const float hb = gate_hidden(s, b1j, g.act);
+    acc_out += bf16_round(act_fn(hb, g.act)) * w2j;
   }
   for (int o = 16; o; o >>= 1) acc_out += __shfl_xor_sync(0xffffffff, acc_out, o);
   if (lane == 0) part[warp] = acc_out;
