@@ -28,6 +28,7 @@ from .layers import (  # noqa: F401
 )
 from .pool import RING_ON_DEVICE, WgkvPool, advance_host_ring, init_pool, ring_to_device  # noqa: F401
 from .prefill import sparse_attn_func, sparse_attn_func_pooled, sparse_attn_func_wrapper  # noqa: F401
+from . import ops  # noqa: F401  (torch.ops.wgkv.paged_decode, torch.ops.wgkv.sparse_attn)
 from .runtime import check_errors  # noqa: F401
 from .tp import KVHeadParallelAttention, shard_gate, shard_o_proj  # noqa: F401
 
