@@ -48,3 +48,21 @@ def test_cpu_tensors_have_no_kernel():
     bt = torch.zeros(1, 2, 1, dtype=torch.int32)
     with pytest.raises(NotImplementedError):
         torch.ops.wgkv.paged_decode(q, kc, kc, sl, bt, 0.1)
+
+
+def test_traced_graph_holds_the_operator():
+    """A function around the decode op traces (fake tensors, no GPU) into a graph with one wgkv node."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def step(q, kc, vc, sl, bt):
+        return torch.ops.wgkv.paged_decode(q * 2, kc, vc, sl, bt, 0.125).float().sum()
+
+    with FakeTensorMode() as mode:
+        args = (torch.empty(2, 1, 8, 64, dtype=torch.bfloat16, device="cuda"),
+                torch.empty(10, 16, 64, dtype=torch.bfloat16, device="cuda"),
+                torch.empty(10, 16, 64, dtype=torch.bfloat16, device="cuda"),
+                torch.empty(2, 2, dtype=torch.int32, device="cuda"),
+                torch.empty(2, 2, 5, dtype=torch.int32, device="cuda"))
+    gm = make_fx(step, tracing_mode="fake")(*args)
+    targets = [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+    assert sum("wgkv.paged_decode" in t for t in targets) == 1
